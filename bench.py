@@ -1,0 +1,343 @@
+#!/usr/bin/env python
+"""Benchmark of the NNop B200 hot path.
+
+Headline: flash_attention forward + backward (gradient of
+sum(o) w.r.t. q, k, v and pair), bf16, E=64, L=4096, H=16, B=8 per GPU,
+causal, additive pair bias (H, QL, KL, B).  Metric: TFLOP/s with the FA2 flop
+convention 14·B·H·L²·E·½ (causal).  Weak scaling: every rank runs its own
+batch slice of B=8 (global batch 8·N), no collective on the data path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line is printed by rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG = ROOT / "onionop.jl_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+CFG = dict(E=64, L=4096, H=16, B=8, causal=True, dtype="bf16")
+METRIC = "attention fwd+bwd TFLOP/s (bf16, L=4096) at 1/2/4/8 B200; norm/RoPE HBM GB/s"
+
+
+def cfg_flops(B, H, L, E, causal):
+    c = 0.5 if causal else 1.0
+    fwd = 4.0 * B * H * L * L * E * c
+    return fwd, 2.5 * fwd
+
+
+def cfg_bytes(B, H, L, E, causal, esz=2):
+    """Algorithmic HBM bytes of one fwd+bwd (dense tensors once each; pair read
+    over the causal half in fwd and bwd; dpair written in full)."""
+    c = 0.5 if causal else 1.0
+    pair = B * H * L * L * esz
+    qkvo = B * H * L * E * esz
+    fwd = c * pair + 3 * qkvo + qkvo                # read q,k,v,pair; write o
+    bwd = c * pair + pair + 5 * qkvo + 3 * qkvo     # read q,k,v,o,dO,pair; write dq,dk,dv,dpair
+    return fwd, bwd
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            if self.uuid and self.uuid not in parts[0]:
+                continue
+            rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# --------------------------------------------------------------- CPU arm
+def cpu_attention_sample(seconds: float = 12.0, max_heads: int = 64):
+    """Oracle port (numpy float32, all host threads via BLAS) on one (batch,
+    head) slice of the headline workload at a time, fwd + bwd, until `seconds`
+    elapse.  Returns (TFLOP/s, heads done, seconds)."""
+    import numpy as np
+    from oracle import nnop_oracle as orc
+    E, L = CFG["E"], CFG["L"]
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, 1, L, E)).astype(np.float32)
+    k = rng.standard_normal((1, 1, L, E)).astype(np.float32)
+    v = rng.standard_normal((1, 1, L, E)).astype(np.float32)
+    pair = rng.standard_normal((1, L, L, 1)).astype(np.float32)
+    do = np.ones((1, 1, L, E), np.float32)
+    scale = orc.attention_scale(E, "bf16")
+    fwd, bwd = cfg_flops(1, 1, L, E, True)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_heads:
+        orc.attention_fwd(q, k, v, pair, causal=True, scale=scale, work_dtype=np.float32)
+        orc.attention_bwd(do, q, k, v, pair, causal=True, scale=scale, work_dtype=np.float32)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return (fwd + bwd) * n / dt / 1e12, n, dt
+
+
+def host_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        return max((i.get("num_threads", 1) for i in info), default=os.cpu_count())
+    except Exception:
+        return os.cpu_count()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    K, W = args.steps, args.warmup
+    import numpy as np  # noqa: F401
+    # each step: one (batch, head) slice of the workload, fwd + bwd
+    per_step = max(1, 1)
+    times = []
+    for i in range(W + K):
+        t0 = time.perf_counter()
+        tf, n, dt = cpu_attention_sample(seconds=0.0, max_heads=per_step)
+        if i >= W:
+            times.append(dt)
+    fwd, bwd = cfg_flops(1, 1, CFG["L"], CFG["E"], True)
+    ms = sum(times) / len(times) * 1e3
+    value = (fwd + bwd) / (ms / 1e3) / 1e12
+    cores = host_threads()
+    sample = f"one (batch, head) slice of config 2 per step (L=4096, E=64, causal, pair), numpy float32"
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 bf16 causal pair-bias FA fwd+bwd, sampled on CPU", "E": 64, "L": 4096,
+                   "H": 16, "B": 8, "causal": True},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (Julia NNop) cannot run here: no Julia toolchain and every kernel is cpu=false; "
+                "this arm times the oracle restatement of its algorithm on the host cores",
+    }
+    print(json.dumps(out), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import nnop
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    E, L, H, B, causal = CFG["E"], CFG["L"], CFG["H"], CFG["B"], CFG["causal"]
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    q = torch.randn(B, H, L, E, device=dev, dtype=dt, generator=g)
+    k = torch.randn(B, H, L, E, device=dev, dtype=dt, generator=g)
+    v = torch.randn(B, H, L, E, device=dev, dtype=dt, generator=g)
+    pair = torch.randn(B, L, L, H, device=dev, dtype=dt, generator=g)
+    do = torch.ones(B, H, L, E, device=dev, dtype=dt)
+
+    def step(q, k, v, pair, do):
+        o, lse = nnop._flash_attention(q, k, v, pair, causal=causal)
+        return o, lse, nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=causal)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step(q, k, v, pair, do)
+    torch.cuda.synchronize(dev)
+
+    # ---- device-resident timing (value)
+    K = args.steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * K)]
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(K):
+        ev[3 * i].record(stream)
+        o, lse = nnop._flash_attention(q, k, v, pair, causal=causal)
+        ev[3 * i + 1].record(stream)
+        nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=causal)
+        ev[3 * i + 2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+    ms_local = t_start.elapsed_time(t_end) / K
+    fwd_ms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(K)) / K
+    bwd_ms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(K)) / K
+    t = torch.tensor([ms_local, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, fwd_ms, bwd_ms = (float(x) for x in t.tolist())
+
+    fwd_f, bwd_f = cfg_flops(B, H, L, E, causal)
+    value = (fwd_f + bwd_f) * world / (ms / 1e3) / 1e12
+
+    # ---- end to end through the public API with host buffers (pinned)
+    del o, lse
+    torch.cuda.empty_cache()
+    host_in = [x.to("cpu").pin_memory() for x in (q, k, v, pair, do)]
+    host_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in (q, k, v, pair)]
+    dev_in = [torch.empty_like(x) for x in (q, k, v, pair, do)]
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = sum(x.numel() * x.element_size() for x in host_out)
+    Ke = max(2, min(K, 5))
+    for _ in range(1):
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        _, _, grads = step(*dev_in)
+        for h_, g_ in zip(host_out, grads):
+            h_.copy_(g_, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(Ke):
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        _, _, grads = step(*dev_in)
+        for h_, g_ in zip(host_out, grads):
+            h_.copy_(g_, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1) / Ke], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    e2e_value = (fwd_f + bwd_f) * world / (e2e_ms / 1e3) / 1e12
+
+    hbm, tc, src = peaks()
+    bwd_bytes = cfg_bytes(B, H, L, E, causal)[1]
+    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    roofline = {
+        "kernel": "flash_attention_bwd call (fa_bwd_mma_kernel + preprocess, dq convert, dpair fill)",
+        "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+        "peak_source": f"{src} hbm_gbs", "traffic": None,
+        "algorithmic_bytes_per_launch": bwd_bytes, "launch_ms": bwd_ms,
+        "tensor_frac_of_step": (fwd_f + bwd_f) / (ms / 1e3) / 1e12 / tc,
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+    }
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tf, n, dt_s = cpu_attention_sample(seconds=args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": host_threads(), "kind": "port",
+               "sample": f"{n} (batch, head) slices of config 2 (L=4096, E=64, causal, pair), fwd+bwd, numpy "
+                         f"float32 oracle port, {dt_s:.1f} s"}
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (q,k,v,pair ~ N(0,1), dO = ones)",
+            "config": {"workload": "config2: flash_attention fwd+bwd bf16 causal + pair bias", "E": E, "L": L,
+                       "H": H, "B_per_gpu": B, "global_batch": B * world, "causal": causal,
+                       "parallelism": f"dp{world} (batch shards, no collective)",
+                       "l2": "inputs larger than L2 (pair 4.29 GB per GPU)"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": K * 5,
+            "roofline": roofline,
+            "clocks": clk,
+        }
+        if cpu is not None:
+            out["cpu_baseline"] = cpu
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,223 @@
+/*
+ * nnop_b200.h -- C ABI of the B200 (sm_100a) implementation of NNop's fused
+ * kernels: flash attention (forward/backward, pair bias, causal, GQA,
+ * key-padding mask), online softmax, RMSNorm, LayerNorm and Llama RoPE.
+ *
+ * Conventions (all entry points)
+ * ------------------------------
+ * - Pointers are DEVICE pointers owned by the caller; the library allocates
+ *   nothing.  Where a kernel needs scratch, a `*_workspace_size` query gives
+ *   the byte count and the caller passes the buffer.
+ * - Dimension names and order follow the reference's column-major Julia arrays.
+ *   A Julia array of size (d1, d2, ..., dn) is the row-major buffer
+ *   [dn]...[d2][d1]; so q (E, QL, QH, B) is the buffer [B][QH][QL][E] and the
+ *   pair bias (H, QL, KL, B) is [B][KL][QL][H].
+ * - `dtype` is one of NNOP_F32 / NNOP_F16 / NNOP_BF16 and applies to every
+ *   floating-point tensor argument unless stated otherwise.  Statistics saved
+ *   for the backward pass (lse, rstd, mean) are always float32.
+ * - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call is
+ *   asynchronous on that stream, like the reference's KernelAbstractions
+ *   launches.
+ * - Return value: NNOP_OK (0) or a negative NNOP_ERR_* code; shape checks happen
+ *   before any launch (as the reference's `error(...)`/`@assert` do) and
+ *   nnop_last_error() returns the message for the calling thread.
+ */
+#ifndef NNOP_B200_H
+#define NNOP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NNOP_B200_ABI_VERSION 1
+
+typedef enum {
+    NNOP_F32 = 0,
+    NNOP_F16 = 1,
+    NNOP_BF16 = 2
+} nnop_dtype_t;
+
+typedef enum {
+    NNOP_OK = 0,
+    NNOP_ERR_SHAPE = -1,       /* inconsistent or unsupported dimensions  */
+    NNOP_ERR_DTYPE = -2,       /* dtype not supported by this entry point */
+    NNOP_ERR_ARG = -3,         /* NULL pointer / bad flag                 */
+    NNOP_ERR_WORKSPACE = -4,   /* workspace missing or too small          */
+    NNOP_ERR_CUDA = -5,        /* CUDA launch / runtime error             */
+    NNOP_ERR_ALIGN = -6        /* pointer not aligned as documented       */
+} nnop_status_t;
+
+/* ABI version (NNOP_B200_ABI_VERSION). */
+int nnop_abi_version(void);
+
+/* Message for the last non-OK status returned on the calling thread. */
+const char* nnop_last_error(void);
+
+/* Fixed text for a status code. */
+const char* nnop_status_string(int status);
+
+/* --------------------------------------------------------------------------
+ * Flash attention
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Forward.  Replaces `_flash_attention` (src/attention.jl:177-229) and its
+ * kernel `_flash_attention_fwd!` (src/attention.jl:40-175).
+ *
+ *   q    [B][QH][QL][E]    (Julia q  (E, QL, QH, B))
+ *   k, v [B][KH][KL][E]    (Julia k, v (E, KL, KH, B)); k and v share a shape
+ *   pair [B][KL][QL][QH]   (Julia pair (QH, QL, KL, B)) or NULL
+ *   kpad_mask [B][KL] uint8 (Julia kpad_mask::Matrix{Bool} (KL, B)) or NULL;
+ *                           nonzero = key is kept
+ *   o    [B][QH][QL][E]    output, dtype
+ *   lse  [B][QH][QL] f32   log-sum-exp of each row's logits; it replaces the
+ *                          reference's (ms, ls) pair: lse = ms + log(ls)
+ *
+ * logits s_ij = scale·(q_i·k_j) [+ pair] with key j masked (−Inf) when
+ * causal && j > i or kpad_mask[b][j] == 0; scale = dtype(1/sqrt(E)).
+ * Checks (src/attention.jl:185-188): E must be a power of two (16..128 here),
+ * QH % KH == 0.  dtype: F32, F16, BF16.
+ */
+int nnop_flash_attention_fwd(const void* q, const void* k, const void* v,
+                             const void* pair, const uint8_t* kpad_mask,
+                             void* o, float* lse,
+                             int64_t E, int64_t QL, int64_t KL,
+                             int64_t QH, int64_t KH, int64_t B,
+                             int causal, int dtype, void* stream);
+
+/* Bytes of workspace nnop_flash_attention_bwd needs for these dimensions. */
+size_t nnop_flash_attention_bwd_workspace_size(int64_t E, int64_t QL, int64_t KL,
+                                               int64_t QH, int64_t KH, int64_t B,
+                                               int dtype);
+
+/*
+ * Backward.  Replaces `∇flash_attention` (src/attention_bwd.jl:213-303) with
+ * its kernels `_flash_attention_bwd_preprocess!` (:177-211) and
+ * `_flash_attention_bwd!` (:1-175).
+ *
+ *   dO [B][QH][QL][E]; o, lse as returned by the forward; q, k, v, pair,
+ *   kpad_mask as given to the forward.
+ *   dq like q, dk/dv like k, dpair like pair (every element written; zero where
+ *   the logit was masked) -- dpair must be NULL iff pair is NULL.
+ *   workspace: >= nnop_flash_attention_bwd_workspace_size(...) bytes,
+ *   256-byte aligned.
+ */
+int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse,
+                             const void* q, const void* k, const void* v,
+                             const void* pair, const uint8_t* kpad_mask,
+                             void* dq, void* dk, void* dv, void* dpair,
+                             void* workspace, size_t workspace_bytes,
+                             int64_t E, int64_t QL, int64_t KL,
+                             int64_t QH, int64_t KH, int64_t B,
+                             int causal, int dtype, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Online softmax over the contiguous axis (Julia dims=1)
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Forward.  Replaces `online_softmax` (src/softmax.jl:60-68) and its kernel
+ * `online_softmax!` (src/softmax.jl:19-58).
+ *   x, y [cols][n]   (Julia x (n, cols)); softmax over each run of n.
+ */
+int nnop_online_softmax_fwd(const void* x, void* y, int64_t n, int64_t cols,
+                            int dtype, void* stream);
+
+/*
+ * Backward.  Replaces `∇online_softmax` (src/softmax.jl:70-80):
+ *   dx = dy∘y − y∘Σ(dy∘y)
+ */
+int nnop_online_softmax_bwd(const void* dy, const void* y, void* dx,
+                            int64_t n, int64_t cols, int dtype, void* stream);
+
+/* --------------------------------------------------------------------------
+ * RMSNorm over the contiguous axis (Julia x (emb, n))
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Forward.  Replaces `_rms_norm` (src/rms_norm.jl:203-223) and `_rms_norm!`
+ * (src/rms_norm.jl:89-124).
+ *   x, y [n][emb] dtype; w [emb] dtype; rstd [n] f32 = 1/sqrt(mean(x²)+eps)
+ *   y = (offset + w)·x·rstd
+ */
+int nnop_rms_norm_fwd(const void* x, const void* w, void* y, float* rstd,
+                      int64_t emb, int64_t n, float eps, float offset,
+                      int dtype, void* stream);
+
+size_t nnop_rms_norm_bwd_workspace_size(int64_t emb, int64_t n);
+
+/*
+ * Backward.  Replaces `∇rms_norm` (src/rms_norm.jl:225-255) and `_∇rms_norm!`
+ * (src/rms_norm.jl:129-201).
+ *   dy, x, dx [n][emb] dtype; w [emb] dtype; rstd [n] f32 (from the forward);
+ *   dw [emb] f32 (the reference returns a Float32 dw as well).
+ */
+int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w,
+                      const float* rstd, void* dx, float* dw,
+                      void* workspace, size_t workspace_bytes,
+                      int64_t emb, int64_t n, float offset,
+                      int dtype, void* stream);
+
+/* --------------------------------------------------------------------------
+ * LayerNorm over the contiguous axis (Julia x (emb, n))
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Forward.  Replaces `_layer_norm` (src/layer_norm.jl:150-170) and
+ * `_layer_norm!` (src/layer_norm.jl:8-63).
+ *   x, y [n][emb], w, b [emb] dtype; mean, rstd [n] f32 (the reference's μ, Σ)
+ */
+int nnop_layer_norm_fwd(const void* x, const void* w, const void* b, void* y,
+                        float* mean, float* rstd, int64_t emb, int64_t n,
+                        float eps, int dtype, void* stream);
+
+size_t nnop_layer_norm_bwd_workspace_size(int64_t emb, int64_t n);
+
+/*
+ * Backward.  Replaces `∇layer_norm` (src/layer_norm.jl:172-204) and
+ * `_∇layer_norm!` (src/layer_norm.jl:65-148).
+ *   dw, db [emb] in dtype (eltype(w) in the reference).
+ */
+int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w,
+                        const float* mean, const float* rstd,
+                        void* dx, void* dw, void* db,
+                        void* workspace, size_t workspace_bytes,
+                        int64_t emb, int64_t n, int dtype, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Llama RoPE
+ * -------------------------------------------------------------------------- */
+
+/*
+ * Rotation of q and k in one launch.  Replaces `_llama_rope`
+ * (src/rope/llama_rope.jl:289-309) and `llama_rope!` (:244-285).
+ *   q, q_out [B][QH][L][E]; k, k_out [B][KH][L][E] (dtype)
+ *   cos, sin [cos_batch][L][E] f32 (Julia (E, L, batch)); cos_batch is B, or
+ *   1 to share one table across the batch.
+ *   sign = +1 forward, -1 backward (∇llama_rope, :312).
+ * For i < E/2: out[i] = x[i]c − x[i+E/2]s, out[i+E/2] = x[i+E/2]c + x[i]s, with
+ * c = cos[i], s = sign·sin[i].  q_out may alias q and k_out may alias k.
+ */
+int nnop_llama_rope(const void* q, const void* k,
+                    const float* cos_t, const float* sin_t,
+                    void* q_out, void* k_out,
+                    int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                    int64_t cos_batch, float sign, int dtype, void* stream);
+
+/*
+ * cos/sin tables of `LlamaRotaryEmbedding(dim; base)(position_ids)`
+ * (src/rope/llama_rope.jl:227-242) computed on the device.
+ *   position_ids [B][L] f32 (Julia (L, B)); cos_t, sin_t [B][L][dim] f32.
+ */
+int nnop_llama_rope_cos_sin(const float* position_ids, float* cos_t, float* sin_t,
+                            int64_t dim, int64_t L, int64_t B, int64_t base,
+                            void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NNOP_B200_H */

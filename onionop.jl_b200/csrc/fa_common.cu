@@ -1,0 +1,130 @@
+// Small memory-bound kernels around the flash-attention backward:
+// * kv_len        : per-batch last kept key (+1) of the key-padding mask;
+// * preprocess    : delta = rowsum(dO ∘ O) in fp32.  The reference computes
+//                   Δs = Δ/l and δ = Σ Δs∘o (src/attention_bwd.jl:177-211); with
+//                   the forward saving a normalised O and lse, δ = rowsum(dO∘O)
+//                   is the same quantity and Δ needs no rescaled copy;
+// * dpair_fill    : zeros of the dpair entries no backward CTA writes (tiles
+//                   above the causal diagonal, fully masked key tiles), written
+//                   head-innermost and coalesced.  The reference zero-fills the
+//                   whole dpair first (`KA.zeros`, src/attention_bwd.jl:250-252);
+//                   here every element is written exactly once;
+// * convert       : fp32 dq accumulator -> dq dtype.
+#include "fa_common.cuh"
+
+namespace nnop {
+namespace {
+
+__global__ void kv_len_kernel(const uint8_t* __restrict__ kmask, int* __restrict__ kv_len, int64_t KL) {
+    const int b = blockIdx.x;
+    const int r = fa::kv_valid_len_block(kmask + (int64_t)b * KL, KL);
+    if (threadIdx.x == 0) kv_len[b] = r;
+}
+
+// One thread per row of E elements; 16-byte vector loads.
+template <typename T, int VEC>
+__global__ void preprocess_kernel(const T* __restrict__ dO, const T* __restrict__ o, float* __restrict__ delta,
+                                  int64_t rows, int E) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const T* a = dO + r * E;
+    const T* c = o + r * E;
+    float s = 0.f;
+    for (int e = 0; e < E; e += VEC) {
+        float av[VEC], cv[VEC];
+        load_vec<T, VEC>(av, a + e);
+        load_vec<T, VEC>(cv, c + e);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) s += av[i] * cv[i];
+    }
+    delta[r] = s;
+}
+
+// One CTA per (batch, key) row of dpair ([QL][QH] contiguous).  The backward
+// kernels write query range [i_lo, QL) of key j; this kernel zeros [0, i_lo).
+template <typename T>
+__global__ void dpair_fill_kernel(T* __restrict__ dpair, const int* __restrict__ kv_len, int64_t QL, int64_t KL,
+                                  int QH, int tile, int causal) {
+    const int64_t row = blockIdx.x;
+    const int64_t b = row / KL, j = row % KL;
+    const int64_t jt = (j / tile) * tile;
+    int64_t i_lo = causal ? jt : 0;
+    if (kv_len != nullptr && jt >= kv_len[b]) i_lo = QL;
+    if (i_lo > QL) i_lo = QL;
+    T* base = dpair + row * QL * QH;
+    const int64_t n = i_lo * QH;
+    // 16-byte stores where the row start allows it.
+    const int64_t head = ((16 - (reinterpret_cast<uintptr_t>(base) & 15)) & 15) / sizeof(T);
+    const int64_t h = head < n ? head : n;
+    for (int64_t x = threadIdx.x; x < h; x += blockDim.x) base[x] = from_f<T>(0.f);
+    constexpr int V = 16 / sizeof(T);
+    const int64_t nv = (n - h) / V;
+    uint4 z = make_uint4(0, 0, 0, 0);
+    uint4* vb = reinterpret_cast<uint4*>(base + h);
+    for (int64_t x = threadIdx.x; x < nv; x += blockDim.x) __stcs(vb + x, z);
+    for (int64_t x = h + nv * V + threadIdx.x; x < n; x += blockDim.x) base[x] = from_f<T>(0.f);
+}
+
+template <typename T>
+__global__ void convert_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n) {
+    const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        float4 f = __ldcs(reinterpret_cast<const float4*>(src + i));
+        dst[i] = from_f<T>(f.x);
+        dst[i + 1] = from_f<T>(f.y);
+        dst[i + 2] = from_f<T>(f.z);
+        dst[i + 3] = from_f<T>(f.w);
+    } else {
+        for (int64_t k = i; k < n; ++k) dst[k] = from_f<T>(src[k]);
+    }
+}
+
+}  // namespace
+
+namespace fa_host {
+
+int launch_kv_len(const uint8_t* kmask, int* kv_len, int64_t KL, int B, cudaStream_t s) {
+    kv_len_kernel<<<B, 256, 0, s>>>(kmask, kv_len, KL);
+    return check_launch("flash_attention kv_len");
+}
+
+template <typename T>
+int launch_preprocess(const T* dO, const T* o, float* delta, int64_t rows, int E, cudaStream_t s) {
+    const unsigned grid = (unsigned)((rows + 127) / 128);
+    constexpr int V = 16 / sizeof(T);
+    if (E % V == 0 && aligned16(dO) && aligned16(o))
+        preprocess_kernel<T, V><<<grid, 128, 0, s>>>(dO, o, delta, rows, E);
+    else
+        preprocess_kernel<T, 1><<<grid, 128, 0, s>>>(dO, o, delta, rows, E);
+    return check_launch("flash_attention_bwd preprocess");
+}
+
+template <typename T>
+int launch_dpair_fill(T* dpair, const int* kv_len, int64_t QL, int64_t KL, int QH, int B, int tile, bool causal,
+                      cudaStream_t s) {
+    if (!causal && kv_len == nullptr) return NNOP_OK;
+    const int64_t rows = (int64_t)B * KL;
+    dpair_fill_kernel<T><<<(unsigned)rows, 256, 0, s>>>(dpair, kv_len, QL, KL, QH, tile, causal ? 1 : 0);
+    return check_launch("flash_attention_bwd dpair fill");
+}
+
+template <typename T>
+int launch_convert(const float* src, T* dst, int64_t n, cudaStream_t s) {
+    const int64_t threads = (n + 3) / 4;
+    convert_kernel<T><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(src, dst, n);
+    return check_launch("flash_attention_bwd dq convert");
+}
+
+template int launch_preprocess<float>(const float*, const float*, float*, int64_t, int, cudaStream_t);
+template int launch_preprocess<__half>(const __half*, const __half*, float*, int64_t, int, cudaStream_t);
+template int launch_preprocess<__nv_bfloat16>(const __nv_bfloat16*, const __nv_bfloat16*, float*, int64_t, int,
+                                              cudaStream_t);
+template int launch_dpair_fill<float>(float*, const int*, int64_t, int64_t, int, int, int, bool, cudaStream_t);
+template int launch_dpair_fill<__half>(__half*, const int*, int64_t, int64_t, int, int, int, bool, cudaStream_t);
+template int launch_dpair_fill<__nv_bfloat16>(__nv_bfloat16*, const int*, int64_t, int64_t, int, int, int, bool,
+                                              cudaStream_t);
+template int launch_convert<__half>(const float*, __half*, int64_t, cudaStream_t);
+template int launch_convert<__nv_bfloat16>(const float*, __nv_bfloat16*, int64_t, cudaStream_t);
+
+}  // namespace fa_host
+}  // namespace nnop

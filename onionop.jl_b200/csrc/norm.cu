@@ -1,0 +1,602 @@
+// RMSNorm and LayerNorm, forward and backward, for sm_100a.
+//
+// Reference: src/rms_norm.jl (kernels :89-201, launchers :203-255) and
+// src/layer_norm.jl (kernels :8-148, launchers :150-204).
+//
+// Design (HBM-bound, 2·N·s bytes forward, 3·N·s backward):
+// * one CTA normalises one row (a Julia column of length emb) at a time; each
+//   thread holds its slice of the row in registers as raw 16-byte vectors, so x
+//   (and dy) are read from HBM exactly once;
+// * reductions are warp shuffles plus one shared-memory stage;
+// * the backward runs a persistent grid (SM count x resident CTAs); a thread
+//   owns the same columns for every row it visits, so dw/db accumulate in
+//   registers, and each CTA writes one fp32 partial row to the workspace.  A
+//   second, deterministic kernel sums the partials over CTAs (the reference
+//   sums a (n/4, emb) partial with `sum(dw; dims=1)`, src/rms_norm.jl:248-253).
+// * rows whose length is not a multiple of the 16-byte vector, or unaligned
+//   base pointers, take the same kernels with a vector width of one element.
+#include "common.cuh"
+
+namespace nnop {
+namespace {
+
+constexpr int kNormBlock = 256;
+constexpr int kMaxNV = 16;  // register-cached vectors per thread
+
+// ---------------------------------------------------------------- RMSNorm fwd
+template <typename T, int VEC, int NV>
+__global__ void __launch_bounds__(kNormBlock)
+rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+               float* __restrict__ rstd_out, int emb, int64_t n, float eps, float offset,
+               float inv_emb) {
+    __shared__ float red[32];
+    const int nvec = emb / VEC;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+        const T* xr = x + row * (int64_t)emb;
+        T* yr = y + row * (int64_t)emb;
+        float ss[1] = {0.f};
+        if constexpr (NV > 0) {
+            Vec<T, VEC> xc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        float f = to_f(xc[i].v[e]);
+                        ss[0] += f * f;
+                    }
+                }
+            }
+            block_sum<1>(ss, red);
+            const float r = 1.0f / sqrtf(ss[0] * inv_emb + eps);
+            if (tid == 0) rstd_out[row] = r;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    float wv[VEC], o[VEC];
+                    load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) o[e] = (offset + wv[e]) * to_f(xc[i].v[e]) * r;
+                    store_vec<T, VEC>(yr + idx * VEC, o);
+                }
+            }
+        } else {
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) ss[0] += xv[e] * xv[e];
+            }
+            block_sum<1>(ss, red);
+            const float r = 1.0f / sqrtf(ss[0] * inv_emb + eps);
+            if (tid == 0) rstd_out[row] = r;
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], wv[VEC], o[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) o[e] = (offset + wv[e]) * xv[e] * r;
+                store_vec<T, VEC>(yr + idx * VEC, o);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- RMSNorm bwd
+// dx = rstd·m + rstd·(−rstd²/N·dd·x), m = dy∘(w+offset), dd = Σ m∘x
+// dw partial += dy∘x·rstd      (src/rms_norm.jl:158-188)
+template <typename T, int VEC, int NV>
+__global__ void __launch_bounds__(kNormBlock)
+rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,
+               const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ partial,
+               int emb, int64_t n, float offset, float inv_emb) {
+    __shared__ float red[32];
+    const int nvec = emb / VEC;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    float* prow = partial + (int64_t)blockIdx.x * emb;
+    if constexpr (NV > 0) {
+        float wo[NV][VEC], dwa[NV][VEC];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int idx = tid + i * nt;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) { wo[i][e] = 0.f; dwa[i][e] = 0.f; }
+            if (idx < nvec) {
+                float wv[VEC];
+                load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) wo[i][e] = wv[e] + offset;
+            }
+        }
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            const T* xr = x + row * (int64_t)emb;
+            const T* dr = dy + row * (int64_t)emb;
+            Vec<T, VEC> xc[NV], dc[NV];
+            float dd[1] = {0.f};
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
+                    dc[i] = ldg_stream<T, VEC>(dr + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) dd[0] += to_f(dc[i].v[e]) * wo[i][e] * to_f(xc[i].v[e]);
+                }
+            }
+            block_sum<1>(dd, red);
+            const float r = rstd[row];
+            const float c = -inv_emb * r * r * dd[0];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    float o[VEC];
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        const float d = to_f(dc[i].v[e]), xv = to_f(xc[i].v[e]);
+                        o[e] = r * (d * wo[i][e]) + r * (c * xv);
+                        dwa[i][e] += d * (xv * r);
+                    }
+                    store_vec<T, VEC>(dx + row * (int64_t)emb + idx * VEC, o);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int idx = tid + i * nt;
+            if (idx < nvec) {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) prow[idx * VEC + e] = dwa[i][e];
+            }
+        }
+    } else {
+        for (int idx = tid; idx < nvec * VEC; idx += nt) prow[idx] = 0.f;
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            const T* xr = x + row * (int64_t)emb;
+            const T* dr = dy + row * (int64_t)emb;
+            float dd[1] = {0.f};
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], dv[VEC], wv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(dv, dr + idx * VEC);
+                load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) dd[0] += dv[e] * (wv[e] + offset) * xv[e];
+            }
+            block_sum<1>(dd, red);
+            const float r = rstd[row];
+            const float c = -inv_emb * r * r * dd[0];
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], dv[VEC], wv[VEC], o[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(dv, dr + idx * VEC);
+                load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    o[e] = r * (dv[e] * (wv[e] + offset)) + r * (c * xv[e]);
+                    prow[idx * VEC + e] += dv[e] * (xv[e] * r);
+                }
+                store_vec<T, VEC>(dx + row * (int64_t)emb + idx * VEC, o);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- LayerNorm fwd
+// Two passes over the register-cached row: mean, then biased variance
+// (src/layer_norm.jl:21-62).
+template <typename T, int VEC, int NV>
+__global__ void __launch_bounds__(kNormBlock)
+ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
+              T* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+              int emb, int64_t n, float eps, float inv_emb) {
+    __shared__ float red[32];
+    const int nvec = emb / VEC;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+        const T* xr = x + row * (int64_t)emb;
+        T* yr = y + row * (int64_t)emb;
+        float s[1] = {0.f};
+        if constexpr (NV > 0) {
+            Vec<T, VEC> xc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) s[0] += to_f(xc[i].v[e]);
+                }
+            }
+            block_sum<1>(s, red);
+            const float mu = s[0] * inv_emb;
+            float v[1] = {0.f};
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        const float c = to_f(xc[i].v[e]) - mu;
+                        v[0] += c * c;
+                    }
+                }
+            }
+            block_sum<1>(v, red);
+            const float r = 1.0f / sqrtf(v[0] * inv_emb + eps);
+            if (tid == 0) { mean_out[row] = mu; rstd_out[row] = r; }
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    float wv[VEC], bv[VEC], o[VEC];
+                    load_vec<T, VEC>(wv, w + idx * VEC);
+                    load_vec<T, VEC>(bv, b + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) o[e] = (to_f(xc[i].v[e]) - mu) * r * wv[e] + bv[e];
+                    store_vec<T, VEC>(yr + idx * VEC, o);
+                }
+            }
+        } else {
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) s[0] += xv[e];
+            }
+            block_sum<1>(s, red);
+            const float mu = s[0] * inv_emb;
+            float v[1] = {0.f};
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) { const float c = xv[e] - mu; v[0] += c * c; }
+            }
+            block_sum<1>(v, red);
+            const float r = 1.0f / sqrtf(v[0] * inv_emb + eps);
+            if (tid == 0) { mean_out[row] = mu; rstd_out[row] = r; }
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], wv[VEC], bv[VEC], o[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(wv, w + idx * VEC);
+                load_vec<T, VEC>(bv, b + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) o[e] = (xv[e] - mu) * r * wv[e] + bv[e];
+                store_vec<T, VEC>(yr + idx * VEC, o);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- LayerNorm bwd
+// c1 = mean(w·dy·xn), c2 = mean(w·dy); dx = (w·dy − (xn·c1 + c2))·rstd;
+// dw += dy·xn; db += dy      (src/layer_norm.jl:94-137)
+template <typename T, int VEC, int NV>
+__global__ void __launch_bounds__(kNormBlock)
+ln_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,
+              const float* __restrict__ mean, const float* __restrict__ rstd,
+              T* __restrict__ dx, float* __restrict__ partial, int emb, int64_t n, float inv_emb) {
+    __shared__ float red[64];
+    const int nvec = emb / VEC;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    float* pw = partial + (int64_t)blockIdx.x * 2 * emb;
+    float* pb = pw + emb;
+    if constexpr (NV > 0) {
+        float wv[NV][VEC], dwa[NV][VEC], dba[NV][VEC];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int idx = tid + i * nt;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) { wv[i][e] = 0.f; dwa[i][e] = 0.f; dba[i][e] = 0.f; }
+            if (idx < nvec) load_vec<T, VEC>(wv[i], w + idx * VEC);
+        }
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            const T* xr = x + row * (int64_t)emb;
+            const T* dr = dy + row * (int64_t)emb;
+            const float mu = mean[row], r = rstd[row];
+            Vec<T, VEC> xc[NV], dc[NV];
+            float c[2] = {0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
+                    dc[i] = ldg_stream<T, VEC>(dr + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        const float xn = (to_f(xc[i].v[e]) - mu) * r;
+                        const float wdy = wv[i][e] * to_f(dc[i].v[e]);
+                        c[0] += wdy * xn;
+                        c[1] += wdy;
+                    }
+                }
+            }
+            block_sum<2>(c, red);
+            const float c1 = c[0] * inv_emb, c2 = c[1] * inv_emb;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    float o[VEC];
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        const float d = to_f(dc[i].v[e]);
+                        const float xn = (to_f(xc[i].v[e]) - mu) * r;
+                        const float wdy = wv[i][e] * d;
+                        o[e] = (wdy - (xn * c1 + c2)) * r;
+                        dwa[i][e] += d * xn;
+                        dba[i][e] += d;
+                    }
+                    store_vec<T, VEC>(dx + row * (int64_t)emb + idx * VEC, o);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int idx = tid + i * nt;
+            if (idx < nvec) {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    pw[idx * VEC + e] = dwa[i][e];
+                    pb[idx * VEC + e] = dba[i][e];
+                }
+            }
+        }
+    } else {
+        for (int idx = tid; idx < nvec * VEC; idx += nt) { pw[idx] = 0.f; pb[idx] = 0.f; }
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            const T* xr = x + row * (int64_t)emb;
+            const T* dr = dy + row * (int64_t)emb;
+            const float mu = mean[row], r = rstd[row];
+            float c[2] = {0.f, 0.f};
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], dv[VEC], wl[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(dv, dr + idx * VEC);
+                load_vec<T, VEC>(wl, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    const float xn = (xv[e] - mu) * r;
+                    const float wdy = wl[e] * dv[e];
+                    c[0] += wdy * xn;
+                    c[1] += wdy;
+                }
+            }
+            block_sum<2>(c, red);
+            const float c1 = c[0] * inv_emb, c2 = c[1] * inv_emb;
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], dv[VEC], wl[VEC], o[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(dv, dr + idx * VEC);
+                load_vec<T, VEC>(wl, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    const float xn = (xv[e] - mu) * r;
+                    o[e] = (wl[e] * dv[e] - (xn * c1 + c2)) * r;
+                    pw[idx * VEC + e] += dv[e] * xn;
+                    pb[idx * VEC + e] += dv[e];
+                }
+                store_vec<T, VEC>(dx + row * (int64_t)emb + idx * VEC, o);
+            }
+        }
+    }
+}
+
+// Column sums of `nparts` fp32 partial rows, each `stride` floats apart; one
+// thread per column, fixed summation order (deterministic).
+template <typename TO>
+__global__ void reduce_partials_kernel(const float* __restrict__ partial, TO* __restrict__ out,
+                                       int emb, int64_t stride, int nparts) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= emb) return;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int g = 0;
+    for (; g + 3 < nparts; g += 4) {
+        s0 += partial[(int64_t)g * stride + c];
+        s1 += partial[(int64_t)(g + 1) * stride + c];
+        s2 += partial[(int64_t)(g + 2) * stride + c];
+        s3 += partial[(int64_t)(g + 3) * stride + c];
+    }
+    for (; g < nparts; ++g) s0 += partial[(int64_t)g * stride + c];
+    out[c] = from_f<TO>((s0 + s1) + (s2 + s3));
+}
+
+// ---------------------------------------------------------------- dispatch
+// Picks the 16-byte vector path when every row starts 16-byte aligned, and the
+// number of cached vectors per thread from the row length.
+struct RowPlan {
+    bool vec;
+    int block;
+    int nv;  // 0 = uncached
+};
+
+template <typename T>
+RowPlan plan_rows(int emb, std::initializer_list<const void*> ptrs) {
+    constexpr int V = 16 / sizeof(T);
+    bool vec = (emb % V == 0);
+    for (const void* p : ptrs) vec = vec && (p == nullptr || aligned16(p));
+    const int nvec = vec ? emb / V : emb;
+    int block = ((nvec + 31) / 32) * 32;
+    if (block > kNormBlock) block = kNormBlock;
+    if (block < 32) block = 32;
+    const int per = (nvec + block - 1) / block;
+    int nv = 1;
+    while (nv < per) nv *= 2;
+    if (nv > kMaxNV) nv = 0;
+    return {vec, block, nv};
+}
+
+#define NNOP_NV_SWITCH(nv, NVC, ...)                         \
+    switch (nv) {                                            \
+        case 1: { constexpr int NVC = 1; __VA_ARGS__; } break;   \
+        case 2: { constexpr int NVC = 2; __VA_ARGS__; } break;   \
+        case 4: { constexpr int NVC = 4; __VA_ARGS__; } break;   \
+        case 8: { constexpr int NVC = 8; __VA_ARGS__; } break;   \
+        case 16: { constexpr int NVC = 16; __VA_ARGS__; } break; \
+        default: { constexpr int NVC = 0; __VA_ARGS__; } break;  \
+    }
+
+#define NNOP_VEC_SWITCH(vec, T, VC, ...)                                      \
+    if (vec) { constexpr int VC = 16 / sizeof(T); __VA_ARGS__; }             \
+    else { constexpr int VC = 1; __VA_ARGS__; }
+
+int64_t rows_grid(int64_t n) { return n < (int64_t)1 << 30 ? n : (int64_t)1 << 30; }
+
+// Persistent backward grid: at most kBwdBlocksPerSm CTAs per SM; the workspace
+// is sized for that bound so its size does not depend on occupancy.
+constexpr int kBwdBlocksPerSm = 8;
+
+template <typename KernelT>
+int bwd_grid(KernelT kernel, int block, int64_t n) {
+    int occ = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, 0) != cudaSuccess || occ < 1) occ = 1;
+    if (occ > kBwdBlocksPerSm) occ = kBwdBlocksPerSm;
+    int64_t g = (int64_t)num_sms() * occ;
+    if (g > n) g = n;
+    if (g < 1) g = 1;
+    return (int)g;
+}
+
+int64_t bwd_max_parts(int64_t n) {
+    int64_t g = (int64_t)num_sms() * kBwdBlocksPerSm;
+    return g < n ? g : (n < 1 ? 1 : n);
+}
+
+int check_norm_args(int64_t emb, int64_t n) {
+    if (emb <= 0 || n < 0) return fail(NNOP_ERR_SHAPE, "norm: emb must be > 0 and n >= 0");
+    if (emb > (int64_t)1 << 24) return fail(NNOP_ERR_SHAPE, "norm: emb too large (max 2^24)");
+    return NNOP_OK;
+}
+
+}  // namespace
+}  // namespace nnop
+
+using namespace nnop;
+
+extern "C" {
+
+int nnop_rms_norm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t emb, int64_t n,
+                      float eps, float offset, int dtype, void* stream) {
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (n == 0) return NNOP_OK;
+    if (!x || !w || !y || !rstd) return fail(NNOP_ERR_ARG, "rms_norm_fwd: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        RowPlan p = plan_rows<T>((int)emb, {x, w, y});
+        NNOP_VEC_SWITCH(p.vec, T, VC, {
+            NNOP_NV_SWITCH(p.nv, NVC, {
+                rms_fwd_kernel<T, VC, NVC><<<(unsigned)rows_grid(n), p.block, 0, s>>>(
+                    (const T*)x, (const T*)w, (T*)y, rstd, (int)emb, n, eps, offset, 1.0f / (float)emb);
+            });
+        });
+    });
+    return check_launch("rms_norm_fwd");
+}
+
+size_t nnop_rms_norm_bwd_workspace_size(int64_t emb, int64_t n) {
+    return (size_t)bwd_max_parts(n) * (size_t)emb * sizeof(float);
+}
+
+int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx,
+                      float* dw, void* workspace, size_t workspace_bytes, int64_t emb, int64_t n,
+                      float offset, int dtype, void* stream) {
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (!dy || !x || !w || !rstd || !dx || !dw) return fail(NNOP_ERR_ARG, "rms_norm_bwd: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n == 0) {
+        if (cudaMemsetAsync(dw, 0, emb * sizeof(float), s) != cudaSuccess)
+            return fail(NNOP_ERR_CUDA, "rms_norm_bwd: memset failed");
+        return NNOP_OK;
+    }
+    if (!workspace || workspace_bytes < nnop_rms_norm_bwd_workspace_size(emb, n))
+        return fail(NNOP_ERR_WORKSPACE, "rms_norm_bwd: workspace too small");
+    float* partial = (float*)workspace;
+    int parts = 0;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx});
+        NNOP_VEC_SWITCH(p.vec, T, VC, {
+            NNOP_NV_SWITCH(p.nv, NVC, {
+                auto kern = rms_bwd_kernel<T, VC, NVC>;
+                parts = bwd_grid(kern, p.block, n);
+                kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, rstd, (T*)dx,
+                                                partial, (int)emb, n, offset, 1.0f / (float)emb);
+            });
+        });
+    });
+    st = check_launch("rms_norm_bwd");
+    if (st) return st;
+    reduce_partials_kernel<float><<<(unsigned)((emb + 255) / 256), 256, 0, s>>>(partial, dw, (int)emb, emb, parts);
+    return check_launch("rms_norm_bwd reduce");
+}
+
+int nnop_layer_norm_fwd(const void* x, const void* w, const void* b, void* y, float* mean, float* rstd,
+                        int64_t emb, int64_t n, float eps, int dtype, void* stream) {
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (n == 0) return NNOP_OK;
+    if (!x || !w || !b || !y || !mean || !rstd) return fail(NNOP_ERR_ARG, "layer_norm_fwd: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        RowPlan p = plan_rows<T>((int)emb, {x, w, b, y});
+        NNOP_VEC_SWITCH(p.vec, T, VC, {
+            NNOP_NV_SWITCH(p.nv, NVC, {
+                ln_fwd_kernel<T, VC, NVC><<<(unsigned)rows_grid(n), p.block, 0, s>>>(
+                    (const T*)x, (const T*)w, (const T*)b, (T*)y, mean, rstd, (int)emb, n, eps,
+                    1.0f / (float)emb);
+            });
+        });
+    });
+    return check_launch("layer_norm_fwd");
+}
+
+size_t nnop_layer_norm_bwd_workspace_size(int64_t emb, int64_t n) {
+    return (size_t)bwd_max_parts(n) * 2 * (size_t)emb * sizeof(float);
+}
+
+int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w, const float* mean,
+                        const float* rstd, void* dx, void* dw, void* db, void* workspace,
+                        size_t workspace_bytes, int64_t emb, int64_t n, int dtype, void* stream) {
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (!dy || !x || !w || !mean || !rstd || !dx || !dw || !db)
+        return fail(NNOP_ERR_ARG, "layer_norm_bwd: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n == 0) {
+        NNOP_DISPATCH_DTYPE(dtype, T, {
+            if (cudaMemsetAsync(dw, 0, emb * sizeof(T), s) != cudaSuccess ||
+                cudaMemsetAsync(db, 0, emb * sizeof(T), s) != cudaSuccess)
+                return fail(NNOP_ERR_CUDA, "layer_norm_bwd: memset failed");
+        });
+        return NNOP_OK;
+    }
+    if (!workspace || workspace_bytes < nnop_layer_norm_bwd_workspace_size(emb, n))
+        return fail(NNOP_ERR_WORKSPACE, "layer_norm_bwd: workspace too small");
+    float* partial = (float*)workspace;
+    int parts = 0;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx});
+        NNOP_VEC_SWITCH(p.vec, T, VC, {
+            NNOP_NV_SWITCH(p.nv, NVC, {
+                auto kern = ln_bwd_kernel<T, VC, NVC>;
+                parts = bwd_grid(kern, p.block, n);
+                kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, mean, rstd,
+                                                (T*)dx, partial, (int)emb, n, 1.0f / (float)emb);
+            });
+        });
+        st = check_launch("layer_norm_bwd");
+        if (st) return st;
+        const unsigned g = (unsigned)((emb + 255) / 256);
+        reduce_partials_kernel<T><<<g, 256, 0, s>>>(partial, (T*)dw, (int)emb, 2 * emb, parts);
+        reduce_partials_kernel<T><<<g, 256, 0, s>>>(partial + emb, (T*)db, (int)emb, 2 * emb, parts);
+    });
+    return check_launch("layer_norm_bwd reduce");
+}
+
+}  // extern "C"
