@@ -17,6 +17,7 @@ pytestmark = pytest.mark.gpu
 
 REF_TOL = {"f32": 1e-3, "f16": 1e-1, "bf16": 1e-1}
 TARGET = {"f32": 1e-5, "f16": 2e-2, "bf16": 2e-2}
+ABS_FLOOR = {"f32": 1e-6, "f16": 1e-3, "bf16": 1e-3}
 
 
 def run_case(B, QH, KH, QL, KL, E, dtype, causal, use_pair, use_mask, seed=0, dO_ones=False,
@@ -70,7 +71,12 @@ def check(got, want, dtype, tag=""):
         tol = REF_TOL[dtype]
         assert isapprox(g, w, atol=tol, rtol=tol), f"{tag} {name}: reference tolerance"
         err = orc.rel_err(g, w)
-        assert err <= TARGET[dtype], f"{tag} {name}: rel err {err:.3e} > {TARGET[dtype]} (max abs {orc.max_abs_err(g, w):.3e})"
+        # Relative error of a tensor that is analytically zero (e.g. dq when a
+        # row sees a single key) compares rounding noise with rounding noise;
+        # there an absolute floor applies: RMS error per element ≤ ABS_FLOOR.
+        floor = ABS_FLOOR[dtype] * np.sqrt(max(g.size, 1))
+        ok = err <= TARGET[dtype] or np.linalg.norm(g - w) <= floor
+        assert ok, f"{tag} {name}: rel err {err:.3e} > {TARGET[dtype]} (max abs {orc.max_abs_err(g, w):.3e})"
 
 
 # test/attention_tests.jl grid (non-causal), reduced over (QL, KL) pairs
