@@ -3,6 +3,8 @@
 // src/attention_bwd.jl:224-227), workspace layout and kernel dispatch.
 #include "fa_common.cuh"
 
+#include <cstdlib>
+
 namespace nnop {
 namespace fa {
 template <typename T> int mma_fwd(const Params& p, bool causal, cudaStream_t s);
@@ -11,11 +13,21 @@ int mma_tile();
 int simt_fwd(const Params& p, bool causal, cudaStream_t s);
 int simt_bwd(const Params& p, bool causal, cudaStream_t s);
 int simt_tile();
+bool sm100_fwd_supported(const Params& p, int dtype);
+int sm100_fwd(const Params& p, int dtype, bool causal, cudaStream_t s);
 }  // namespace fa
 
 namespace {
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// NNOP_B200_FA=mma selects the mma.sync kernels for every shape (used by the
+// tests to check both kernel families); the default picks the tcgen05 kernels
+// where they apply.
+bool force_mma() {
+    const char* e = getenv("NNOP_B200_FA");
+    return e != nullptr && e[0] == 'm';
+}
 
 int check_dims(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_t B, int dtype) {
     if (dtype != NNOP_F32 && dtype != NNOP_F16 && dtype != NNOP_BF16)
@@ -88,9 +100,11 @@ int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const 
             return fa::simt_fwd(p, causal != 0, s);
         case NNOP_F16:
             p.scale = __half2float(__float2half_rn((float)(1.0 / sqrt((double)E))));
+            if (!force_mma() && fa::sm100_fwd_supported(p, dtype)) return fa::sm100_fwd(p, dtype, causal != 0, s);
             return fa::mma_fwd<__half>(p, causal != 0, s);
         case NNOP_BF16:
             p.scale = __bfloat162float(__float2bfloat16_rn((float)(1.0 / sqrt((double)E))));
+            if (!force_mma() && fa::sm100_fwd_supported(p, dtype)) return fa::sm100_fwd(p, dtype, causal != 0, s);
             return fa::mma_fwd<__nv_bfloat16>(p, causal != 0, s);
     }
     return fail(NNOP_ERR_DTYPE, "flash_attention_fwd: unsupported dtype");
