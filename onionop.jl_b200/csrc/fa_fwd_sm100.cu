@@ -10,6 +10,13 @@
 //              O += P_j·V_j with P_j read from TMEM (tcgen05 "ts" form);
 //   warps 2-3  tile provider: key-validity bits (padding mask, ragged tail)
 //              and the pair-bias tile, rearranged to [key/8][query][8];
+//              with XC > 0 the XC = H CTAs of one (q-tile, batch) form a
+//              thread-block cluster and share the pair bias: CTA r TMA-loads
+//              keys [r·BN/H, (r+1)·BN/H) of the tile for ALL heads (the pair is
+//              head-innermost, so this is one dense box), transposes it in
+//              registers and pushes each head's slab into that head's CTA with
+//              st.async (peer shared memory, completing the peer's mbarrier
+//              transaction count) -- every pair byte crosses L2 once;
 //   warps 4-7  softmax: thread r owns query row r (TMEM lane r): it reads
 //              its 128 scores, adds the pair bias, masks, updates the running
 //              max (rescaling O in TMEM only when the max grows by more than
@@ -20,6 +27,9 @@
 // Every mbarrier wait is bounded (sm100::wait); on a timeout all roles stop,
 // the CTA frees its TMEM and returns.
 #include <cuda.h>
+
+#include <cstdlib>
+#include <cstring>
 
 #include "fa_common.cuh"
 #include "sm100.cuh"
@@ -47,7 +57,9 @@ enum Bar {
     kTileFull = 13,  // +buffer (provider -> softmax)
     kTileEmpty = 15, // +buffer (softmax -> provider)
     kMmaDone = 17,   // MMA warp's own "all my MMAs retired" barrier
-    kNumBars = 18
+    kStageFull = 18, // exchange: own slice of the all-heads pair box landed
+    kPairEmpty = 19, // +buffer, exchange: every receiver consumed the slot
+    kNumBars = 21
 };
 
 template <int E, bool PAIR>
@@ -59,7 +71,9 @@ struct Layout {
     static constexpr int kV = kK + kStages * kKVBytes;
     static constexpr int kPairBytes = PAIR ? kBN * kBM * 2 : 0;
     static constexpr int kPair = kV + kStages * kKVBytes;
-    static constexpr int kBits = kPair + 2 * kPairBytes;        // 2 x (kBN/32) uint32
+    static constexpr int kStage = kPair + 2 * kPairBytes;       // exchange staging box [BN/H][BM][H]
+    static constexpr int kStageBytes = PAIR ? kBN * kBM * 2 : 0;
+    static constexpr int kBits = kStage + kStageBytes;          // 2 x (kBN/32) uint32
     static constexpr int kBar = kBits + 2 * (kBN / 32) * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kTotal = kTmemSlot + 16;
@@ -92,10 +106,11 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
     for (int i = 0; i < 8; ++i) f[i] = to_f(h[i]);
 }
 
-template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
+template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK, int XC>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_pair,
+                    const Params p) {
     using L = Layout<E, PAIR>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr bool kProvider = PAIR || MASK;
@@ -108,8 +123,8 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t QL = p.QL, KL = p.KL;
     const int n_qt = (int)((QL + kBM - 1) / kBM);
-    const int qt = CAUSAL ? n_qt - 1 - (int)blockIdx.x : (int)blockIdx.x;
-    const int h = blockIdx.y, b = blockIdx.z;
+    const int qt = CAUSAL ? n_qt - 1 - (int)blockIdx.y : (int)blockIdx.y;
+    const int h = blockIdx.x, b = blockIdx.z;
     const int kvh = h / p.n_rep;
     const int64_t q0 = (int64_t)qt * kBM;
     const uint8_t* mg = MASK ? p.kmask + (int64_t)b * KL : nullptr;
@@ -133,9 +148,11 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars[kSFull + i], 1);
             mbar_init(&bars[kPFull + i], 128);
-            mbar_init(&bars[kTileFull + i], 64);
+            mbar_init(&bars[kTileFull + i], XC ? 1 : 64);
             mbar_init(&bars[kTileEmpty + i], 128);
+            mbar_init(&bars[kPairEmpty + i], XC ? XC : 1);
         }
+        mbar_init(&bars[kStageFull], 1);
         mbar_init(&bars[kOFinal], 1);
         mbar_init(&bars[kOStep], 1);
         mbar_init(&bars[kMmaDone], 1);
@@ -147,6 +164,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     tc_fence_before();
     __syncthreads();
+    if (XC) cluster_sync();   // peers' barriers are initialised before any remote access
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS0 = tmem, tS1 = tmem + kBN, tO = tmem + 2 * kBN;
@@ -240,7 +258,76 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         }
     } else if (warp < 4) {
         // ------------------------------------------------------ tile provider
-        if (kProvider) {
+        if constexpr (XC > 0) {
+            // ---- cluster exchange of the pair bias (see header comment)
+            constexpr int KS = kBN / XC;   // keys this CTA stages per tile
+            const int tp = threadIdx.x - 64;
+            const uint32_t rank = cluster_rank();
+            const uint8_t* stage = smem + L::kStage;
+            const uint32_t recv0 = smem_u32(smem + L::kPair);
+            for (int j = 0; j < n_kt; ++j) {
+                const int buf = j & 1;
+                const int64_t k0 = (int64_t)j * kBN;
+                if (j >= 2) {
+                    // my softmax is done with slot `buf` (tile j-2): tell every sender
+                    if (!wait(&bars[kTileEmpty + buf], ((j >> 1) - 1) & 1)) break;
+                    if (tp == 0) {
+                        const uint32_t eb = smem_u32(&bars[kPairEmpty + buf]);
+                        for (int d = 0; d < XC; ++d) mbar_arrive_remote(mapa(eb, d));
+                    }
+                    // and every receiver is done with it before I overwrite it
+                    if (!wait_cluster(&bars[kPairEmpty + buf], ((j >> 1) - 1) & 1)) break;
+                }
+                if (tp == 0) {
+                    mbar_expect_tx(&bars[kStageFull], L::kStageBytes);
+                    tma_load_4d(smem + L::kStage, &tm_pair, &bars[kStageFull], 0, (int)q0, (int)(k0 + rank * KS), b);
+                }
+                if (tp < kBN / 32) {
+                    uint32_t w = 0;
+                    for (int t = 0; t < 32; ++t) {
+                        const int64_t key = k0 + tp * 32 + t;
+                        bool v = key < KL;
+                        if (MASK && v) v = mg[key] != 0;
+                        w |= (v ? 1u : 0u) << t;
+                    }
+                    bits[buf * (kBN / 32) + tp] = w;
+                }
+                if (!wait(&bars[kStageFull], j & 1)) break;
+                named_bar_sync(1, 64);
+                if (tp == 0) mbar_expect_tx_cluster(&bars[kTileFull + buf], kBN * kBM * 2);
+                const uint32_t full_bar = smem_u32(&bars[kTileFull + buf]);
+#pragma unroll 1
+                for (int rr = 0; rr < kBM / 64; ++rr) {
+                    const int q = tp + rr * 64;
+#pragma unroll
+                    for (int kk = 0; kk < KS / 8; ++kk) {
+                        // in[k][w]: keys kk*8+k of query q, word w = heads (2w, 2w+1)
+                        uint32_t in[8][XC / 2];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const uint4* src = reinterpret_cast<const uint4*>(stage + (((kk * 8 + k) * kBM + q) * XC) * 2);
+#pragma unroll
+                            for (int v = 0; v < XC / 8; ++v) {
+                                const uint4 u = src[v];
+                                in[k][4 * v] = u.x; in[k][4 * v + 1] = u.y; in[k][4 * v + 2] = u.z; in[k][4 * v + 3] = u.w;
+                            }
+                        }
+                        const uint32_t off = (uint32_t)(((rank * KS / 8 + kk) * kBM + q) * 16);
+#pragma unroll
+                        for (int hd = 0; hd < XC; ++hd) {
+                            const uint32_t sel = (hd & 1) ? 0x7632u : 0x5410u;
+                            uint4 o;
+                            o.x = __byte_perm(in[0][hd >> 1], in[1][hd >> 1], sel);
+                            o.y = __byte_perm(in[2][hd >> 1], in[3][hd >> 1], sel);
+                            o.z = __byte_perm(in[4][hd >> 1], in[5][hd >> 1], sel);
+                            o.w = __byte_perm(in[6][hd >> 1], in[7][hd >> 1], sel);
+                            st_async16(mapa(recv0 + buf * L::kPairBytes + off, hd), o, mapa(full_bar, hd));
+                        }
+                    }
+                }
+                named_bar_sync(1, 64);   // staging reads done before the next TMA overwrites it
+            }
+        } else if (kProvider) {
             const int tp = threadIdx.x - 64;
             const T* pg = PAIR ? reinterpret_cast<const T*>(p.pair) + (int64_t)b * KL * QL * p.QH + h : nullptr;
             for (int j = 0; j < n_kt; ++j) {
@@ -289,7 +376,11 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int j = 0; j < n_kt; ++j) {
             const int buf = j & 1;
             const int64_t k0 = (int64_t)j * kBN;
-            if (kProvider && !wait(&bars[kTileFull + buf], (j >> 1) & 1)) { ok = false; break; }
+            if (kProvider) {
+                const bool got = XC ? wait_cluster(&bars[kTileFull + buf], (j >> 1) & 1)
+                                    : wait(&bars[kTileFull + buf], (j >> 1) & 1);
+                if (!got) { ok = false; break; }
+            }
             if (!wait(&bars[kSFull + buf], (j >> 1) & 1)) { ok = false; break; }
             tc_fence_after();
             const uint32_t tS = (buf ? tS1 : tS0) + lane_off;
@@ -407,6 +498,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+    if (XC) cluster_sync();   // no peer may still write into this CTA's shared memory
 }
 
 // ---------------------------------------------------------------- host side
@@ -440,30 +532,85 @@ bool make_map(CUtensorMap* m, const void* base, int E, int64_t rows, int64_t bh,
     return r == CUDA_SUCCESS;
 }
 
-template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
-int launch(const Params& p, cudaStream_t s) {
+// 4-D map over the pair bias [B][KL][QL][H] (Julia (H, QL, KL, B)), box
+// (H, BM, BN/H, 1): one CTA's key slice of a tile for every head, no swizzle.
+bool make_pair_map(CUtensorMap* m, const void* base, int H, int64_t QL, int64_t KL, int64_t B, int keys, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)H, (cuuint64_t)QL, (cuuint64_t)KL, (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)H * 2, (cuuint64_t)QL * H * 2, (cuuint64_t)KL * QL * H * 2};
+    cuuint32_t box[4] = {(cuuint32_t)H, (cuuint32_t)kBM, (cuuint32_t)keys, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// NNOP_B200_PAIR_XCH=0 disables the cluster exchange (the gather provider
+// then reads the pair bias per head); used by the tests to cover both.
+bool xch_enabled() {
+    const char* e = getenv("NNOP_B200_PAIR_XCH");
+    return !(e != nullptr && e[0] == '0');
+}
+
+template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK, int XC>
+int launch(const Params& p, cudaStream_t s, bool* launched) {
     using Lay = Layout<E, PAIR>;
     constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-    CUtensorMap tq, tk, tv;
+    *launched = false;
+    CUtensorMap tq, tk, tv, tp;
+    memset(&tp, 0, sizeof(tp));
     if (!make_map(&tq, p.q, E, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
-        !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16))
+        !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
+        (XC && !make_pair_map(&tp, p.pair, p.QH, p.QL, p.KL, p.B, kBN / XC, bf16)))
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cuTensorMapEncodeTiled failed");
-    auto kern = fa_fwd_sm100_kernel<T, E, CAUSAL, PAIR, MASK>;
+    auto kern = fa_fwd_sm100_kernel<T, E, CAUSAL, PAIR, MASK, XC>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cannot set shared memory size");
-    dim3 grid((unsigned)((p.QL + kBM - 1) / kBM), p.QH, p.B);
-    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.QH, (unsigned)((p.QL + kBM - 1) / kBM), p.B);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Lay::kAlloc;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (XC) {
+        if (XC > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = XC;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg) != cudaSuccess || nclusters < 1) {
+            cudaGetLastError();
+            return NNOP_OK;   // not launchable here: caller falls back to the gather provider
+        }
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, tp, p);
+    if (e != cudaSuccess) return fail(NNOP_ERR_CUDA, std::string("flash_attention_fwd (sm100): ") + cudaGetErrorString(e));
+    *launched = true;
     return check_launch("flash_attention_fwd (sm100)");
 }
 
 template <typename T, int E, bool CAUSAL>
 int dispatch_flags(const Params& p, cudaStream_t s) {
     const bool pair = p.pair != nullptr, mask = p.kmask != nullptr;
-    if (pair && mask) return launch<T, E, CAUSAL, true, true>(p, s);
-    if (pair) return launch<T, E, CAUSAL, true, false>(p, s);
-    if (mask) return launch<T, E, CAUSAL, false, true>(p, s);
-    return launch<T, E, CAUSAL, false, false>(p, s);
+    bool done = false;
+    int st = NNOP_OK;
+    if (pair && xch_enabled() && (p.QH == 8 || p.QH == 16) && E == 64) {
+        if (p.QH == 16)
+            st = mask ? launch<T, E, CAUSAL, true, true, 16>(p, s, &done) : launch<T, E, CAUSAL, true, false, 16>(p, s, &done);
+        else
+            st = mask ? launch<T, E, CAUSAL, true, true, 8>(p, s, &done) : launch<T, E, CAUSAL, true, false, 8>(p, s, &done);
+        if (st || done) return st;
+    }
+    if (pair && mask) return launch<T, E, CAUSAL, true, true, 0>(p, s, &done);
+    if (pair) return launch<T, E, CAUSAL, true, false, 0>(p, s, &done);
+    if (mask) return launch<T, E, CAUSAL, false, true, 0>(p, s, &done);
+    return launch<T, E, CAUSAL, false, false, 0>(p, s, &done);
 }
 
 }  // namespace
