@@ -15,6 +15,9 @@ int simt_bwd(const Params& p, bool causal, cudaStream_t s);
 int simt_tile();
 bool sm100_fwd_supported(const Params& p, int dtype);
 int sm100_fwd(const Params& p, int dtype, bool causal, cudaStream_t s);
+bool sm100_bwd_supported(const Params& p, int dtype);
+int sm100_bwd(const Params& p, int dtype, bool causal, cudaStream_t s);
+int sm100_bwd_tile();
 }  // namespace fa
 
 namespace {
@@ -182,23 +185,25 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, co
             if (cudaMemsetAsync(ws.dq_acc, 0, (size_t)rows * E * sizeof(float), s) != cudaSuccess)
                 return fail(NNOP_ERR_CUDA, "flash_attention_bwd: memset failed");
             p.dq_acc = ws.dq_acc;
+            const bool tc = !force_mma() && fa::sm100_bwd_supported(p, dtype);
+            const int tile = tc ? fa::sm100_bwd_tile() : fa::mma_tile();
             if (dtype == NNOP_F16) {
                 p.scale = __half2float(__float2half_rn((float)(1.0 / sqrt((double)E))));
                 st = fa_host::launch_preprocess<__half>((const __half*)dO, (const __half*)o, ws.delta, rows, (int)E, s);
-                if (!st) st = fa::mma_bwd<__half>(p, c, s);
+                if (!st) st = tc ? fa::sm100_bwd(p, dtype, c, s) : fa::mma_bwd<__half>(p, c, s);
                 if (!st) st = fa_host::launch_convert<__half>(ws.dq_acc, (__half*)dq, rows * E, s);
                 if (!st && pair)
                     st = fa_host::launch_dpair_fill<__half>((__half*)dpair, p.kv_len, QL, KL, (int)QH, (int)B,
-                                                            fa::mma_tile(), c, s);
+                                                            tile, c, s);
             } else {
                 p.scale = __bfloat162float(__float2bfloat16_rn((float)(1.0 / sqrt((double)E))));
                 st = fa_host::launch_preprocess<__nv_bfloat16>((const __nv_bfloat16*)dO, (const __nv_bfloat16*)o,
                                                                ws.delta, rows, (int)E, s);
-                if (!st) st = fa::mma_bwd<__nv_bfloat16>(p, c, s);
+                if (!st) st = tc ? fa::sm100_bwd(p, dtype, c, s) : fa::mma_bwd<__nv_bfloat16>(p, c, s);
                 if (!st) st = fa_host::launch_convert<__nv_bfloat16>(ws.dq_acc, (__nv_bfloat16*)dq, rows * E, s);
                 if (!st && pair)
                     st = fa_host::launch_dpair_fill<__nv_bfloat16>((__nv_bfloat16*)dpair, p.kv_len, QL, KL, (int)QH,
-                                                                   (int)B, fa::mma_tile(), c, s);
+                                                                   (int)B, tile, c, s);
             }
             return st;
         }
