@@ -161,6 +161,28 @@ int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w,
                       int64_t emb, int64_t n, float offset,
                       int dtype, void* stream);
 
+/*
+ * RMSNorm backward that allocates nothing.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory where they need the
+ * gradient -- code running inside a memory pool's own callbacks, runtimes that
+ * plan all device memory ahead of time, hosts without access to an allocator
+ * at the call site -- and so cannot pass the workspace nnop_rms_norm_bwd needs.
+ * Same arguments and results as nnop_rms_norm_bwd without the workspace.
+ *
+ * The scratch is an 8 MiB array inside the library (held on every GPU that
+ * loads it until the process exits); emb may be at most 2^21 (2,097,152),
+ * larger values return NNOP_ERR_SHAPE.  The first call on a device looks the
+ * array's device address up (cudaGetSymbolAddress), so make that first call
+ * before any stream capture on that device.  All calls on a device share the
+ * one array: calls that can overlap on the GPU (different streams without
+ * ordering between them) race on it and must be serialised by the caller.
+ */
+int nnop_rms_norm_bwd_noalloc(const void* dy, const void* x, const void* w,
+                              const float* rstd, void* dx, float* dw,
+                              int64_t emb, int64_t n, float offset,
+                              int dtype, void* stream);
+
 /* --------------------------------------------------------------------------
  * LayerNorm over the contiguous axis (Julia x (emb, n))
  * -------------------------------------------------------------------------- */

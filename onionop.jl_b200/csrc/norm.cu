@@ -17,6 +17,8 @@
 //   base pointers, take the same kernels with a vector width of one element.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace nnop {
 namespace {
 
@@ -597,6 +599,92 @@ int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w, const floa
         reduce_partials_kernel<T><<<g, 256, 0, s>>>(partial + emb, (T*)db, (int)emb, 2 * emb, parts);
     });
     return check_launch("layer_norm_bwd reduce");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// RMSNorm backward without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they need the
+// gradient: code that runs inside a memory pool's own callbacks, runtimes that
+// plan every byte of device memory ahead of time, or embedded hosts whose
+// allocator is not reachable from the call site.  They cannot provide the
+// workspace that nnop_rms_norm_bwd needs, so this variant keeps its scratch
+// (the per-CTA fp32 dw partial rows) in a fixed-size array that lives in the
+// library itself.  The array occupies kNoAllocScratchBytes on every GPU that
+// loads the library, for the life of the process.
+// ---------------------------------------------------------------------------
+namespace nnop {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;   // 8 MiB: 2^21 fp32 partials
+constexpr int64_t kNoAllocScratchFloats = (int64_t)(kNoAllocScratchBytes / sizeof(float));
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+// Device address of g_noalloc_scratch for the current device, looked up once
+// per device (the host-side symbol is only a stand-in, never a device pointer).
+int noalloc_scratch(float** out) {
+    static std::mutex mu;
+    static float* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(NNOP_ERR_CUDA, "rms_norm_bwd_noalloc: no current CUDA device");
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(NNOP_ERR_CUDA, std::string("rms_norm_bwd_noalloc: cudaGetSymbolAddress failed: ") +
+                                           cudaGetErrorString(e));
+        addr[dev] = static_cast<float*>(p);
+    }
+    *out = addr[dev];
+    return NNOP_OK;
+}
+
+}  // namespace
+}  // namespace nnop
+
+extern "C" {
+
+int nnop_rms_norm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw,
+                              int64_t emb, int64_t n, float offset, int dtype, void* stream) {
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (emb > kNoAllocScratchFloats)
+        return fail(NNOP_ERR_SHAPE, "rms_norm_bwd_noalloc: emb " + std::to_string(emb) + " exceeds the maximum " +
+                                        std::to_string(kNoAllocScratchFloats) + " of the built-in scratch");
+    if (!dy || !x || !w || !rstd || !dx || !dw) return fail(NNOP_ERR_ARG, "rms_norm_bwd_noalloc: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n == 0) {
+        if (cudaMemsetAsync(dw, 0, emb * sizeof(float), s) != cudaSuccess)
+            return fail(NNOP_ERR_CUDA, "rms_norm_bwd_noalloc: memset failed");
+        return NNOP_OK;
+    }
+    float* partial = nullptr;
+    st = noalloc_scratch(&partial);
+    if (st) return st;
+    // Every partial row the reduction reads is fully written by its CTA first,
+    // so the scratch left over from an earlier call needs no clearing.
+    const int64_t max_parts = kNoAllocScratchFloats / emb;
+    int parts = 0;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx});
+        NNOP_VEC_SWITCH(p.vec, T, VC, {
+            NNOP_NV_SWITCH(p.nv, NVC, {
+                auto kern = rms_bwd_kernel<T, VC, NVC>;
+                parts = bwd_grid(kern, p.block, n);
+                if (parts > max_parts) parts = (int)max_parts;
+                kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, rstd, (T*)dx, partial,
+                                                (int)emb, n, offset, 1.0f / (float)emb);
+            });
+        });
+    });
+    st = check_launch("rms_norm_bwd_noalloc");
+    if (st) return st;
+    reduce_partials_kernel<float><<<(unsigned)((emb + 255) / 256), 256, 0, s>>>(partial, dw, (int)emb, emb, parts);
+    return check_launch("rms_norm_bwd_noalloc reduce");
 }
 
 }  // extern "C"

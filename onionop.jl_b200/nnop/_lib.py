@@ -38,6 +38,7 @@ SIGNATURES = {
     "nnop_rms_norm_fwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f, _f, _int, _vp]),
     "nnop_rms_norm_bwd_workspace_size": (_sz, [_i64, _i64]),
     "nnop_rms_norm_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _f, _int, _vp]),
+    "nnop_rms_norm_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _vp]),
     "nnop_layer_norm_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _vp]),
     "nnop_layer_norm_bwd_workspace_size": (_sz, [_i64, _i64]),
     "nnop_layer_norm_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
