@@ -59,6 +59,17 @@ const char* nnop_last_error(void);
 /* Fixed text for a status code. */
 const char* nnop_status_string(int status);
 
+/*
+ * Diagnostic (no counterpart in the reference, whose kernels have no waits):
+ * every mbarrier wait inside the tcgen05 attention kernels gives up after about
+ * one second and records it in a device flag instead of hanging the GPU.  This
+ * call synchronises the current device, returns the wait sites that recorded a
+ * timeout since the last call (bits 0-15: forward kernel, bits 16-30: backward
+ * kernel, one bit per wait site) and clears the flags.  Non-zero means the
+ * results of those launches are not valid.
+ */
+int nnop_device_wait_timeouts(void);
+
 /* --------------------------------------------------------------------------
  * Flash attention
  * -------------------------------------------------------------------------- */

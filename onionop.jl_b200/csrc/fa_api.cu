@@ -18,6 +18,8 @@ int sm100_fwd(const Params& p, int dtype, bool causal, cudaStream_t s);
 bool sm100_bwd_supported(const Params& p, int dtype);
 int sm100_bwd(const Params& p, int dtype, bool causal, cudaStream_t s);
 int sm100_bwd_tile();
+int sm100_fwd_timeouts();
+int sm100_bwd_timeouts();
 }  // namespace fa
 
 namespace {
@@ -82,6 +84,12 @@ BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t QH, int64_t B
 using namespace nnop;
 
 extern "C" {
+
+int nnop_device_wait_timeouts(void) {
+    const int f = fa::sm100_fwd_timeouts();
+    const int b = fa::sm100_bwd_timeouts();
+    return (f & 0xffff) | ((b & 0x7fff) << 16);
+}
 
 int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const void* pair,
                              const uint8_t* kpad_mask, void* o, float* lse, int64_t E, int64_t QL, int64_t KL,

@@ -109,7 +109,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int nq = (k0 < kv_len && qt0 < n_qt) ? n_qt - qt0 : 0;
     const int steps = nq * p.n_rep;
 
+    __shared__ int s_abort;   // set by the first wait of this CTA that gives up
+    volatile int* ab = &s_abort;
     if (threadIdx.x == 0) {
+        s_abort = 0;
         mbar_init(&bars[kKVFull], 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars[kQFull + s], 1);
@@ -148,7 +151,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             int issued = 0;
             for (int st = 0; st < steps; ++st) {
                 const int s = st & 1;
-                if (st >= 2 && !wait(&bars[kQEmpty + s], ((st >> 1) - 1) & 1)) break;
+                if (st >= 2 && !wait(&bars[kQEmpty + s], ((st >> 1) - 1) & 1, ab, 1)) break;
                 issued = st + 1;
                 const int h = kvh * p.n_rep + st / nq;
                 const int q0 = (qt0 + st % nq) * kBM;
@@ -157,9 +160,9 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tma_load_3d(smem + Lay::kDO + s * Lay::kTile, &tm_do, &bars[kQFull + s], 0, q0, b * QH + h);
             }
             // copies in flight land before the CTA leaves (bounded waits)
-            wait(&bars[kKVFull], 0);
+            wait(&bars[kKVFull], 0, ab, 2);
             for (int st = issued - 2 < 0 ? 0 : issued - 2; st < issued; ++st)
-                wait(&bars[kQFull + (st & 1)], (st >> 1) & 1);
+                wait(&bars[kQFull + (st & 1)], (st >> 1) & 1, ab, 3);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -168,10 +171,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t id_q = idesc_f16<kBF16>(128, 64, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
         const uint32_t sDS = smem_u32(smem + Lay::kDS);
-        bool ok = steps > 0 && wait(&bars[kKVFull], 0);
+        bool ok = steps > 0 && wait(&bars[kKVFull], 0, ab, 4);
         for (int st = 0; ok && st < steps; ++st) {
             const int s = st & 1;
-            if (!wait(&bars[kQFull + s], (st >> 1) & 1)) break;
+            if (!wait(&bars[kQFull + s], (st >> 1) & 1, ab, 5)) break;
             tc_fence_after();
             const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile);
             const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile);
@@ -184,7 +187,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 umma_commit(&bars[kSFull]);
             }
             __syncwarp();
-            if (!wait(&bars[kPFull], st & 1)) break;
+            if (!wait(&bars[kPFull], st & 1, ab, 6)) break;
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
@@ -198,7 +201,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 umma_commit(&bars[kQEmpty + s]);
             }
             __syncwarp();
-            if (st > 0 && !wait(&bars[kDQEmpty], (st - 1) & 1)) break;
+            if (st > 0 && !wait(&bars[kDQEmpty], (st - 1) & 1, ab, 7)) break;
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
@@ -212,13 +215,13 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         // every MMA this warp issued retires before TMEM is read out / freed
         if (lane == 0) umma_commit(&bars[kFinal]);
         __syncwarp();
-        wait(&bars[kFinal], 0);
+        wait(&bars[kFinal], 0, ab, 8);
     } else if (warp < 4) {
         // ------------------------------------------------------ tile provider
         const int tp = threadIdx.x - 64;
         for (int st = 0; st < steps; ++st) {
             const int buf = st & 1;
-            if (st >= 2 && !wait(&bars[kTileEmpty + buf], ((st >> 1) - 1) & 1)) break;
+            if (st >= 2 && !wait(&bars[kTileEmpty + buf], ((st >> 1) - 1) & 1, ab, 9)) break;
             const int h = kvh * p.n_rep + st / nq;
             const int64_t q0 = (int64_t)(qt0 + st % nq) * kBM;
             const int64_t ro = ((int64_t)b * QH + h) * QL;
@@ -262,8 +265,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const int buf = st & 1;
             const int h = kvh * p.n_rep + st / nq;
             const int64_t q0 = (int64_t)(qt0 + st % nq) * kBM;
-            if (!wait(&bars[kTileFull + buf], (st >> 1) & 1)) break;
-            if (!wait(&bars[kSFull], st & 1)) break;
+            if (!wait(&bars[kTileFull + buf], (st >> 1) & 1, ab, 10)) break;
+            if (!wait(&bars[kSFull], st & 1, ab, 11)) break;
             tc_fence_after();
             uint16_t* dpg = PAIR ? reinterpret_cast<uint16_t*>(p.dpair) + (int64_t)b * KL * QL * QH + h : nullptr;
 #pragma unroll 1
@@ -334,7 +337,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             mbar_arrive(&bars[kPFull]);
         }
         // epilogue: dK (warpgroup 0) and dV (warpgroup 1) rows of this CTA's keys
-        if (wait(&bars[kFinal], 0)) {
+        if (wait(&bars[kFinal], 0, ab, 12)) {
             tc_fence_after();
             const bool is_dk = c0 == 0;
             const uint32_t src = (is_dk ? tDK : tDV) + lane_off;
@@ -364,7 +367,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int st = 0; st < steps; ++st) {
             const int h = kvh * p.n_rep + st / nq;
             const int64_t i = (int64_t)(qt0 + st % nq) * kBM + r;
-            if (!wait(&bars[kDQFull], st & 1)) break;
+            if (!wait(&bars[kDQFull], st & 1, ab, 13)) break;
             tc_fence_after();
             float* dq = p.dq_acc + (((int64_t)b * QH + h) * QL + i) * kE;
 #pragma unroll
@@ -425,6 +428,14 @@ bool sm100_bwd_supported(const Params& p, int dtype) {
 }
 
 int sm100_bwd_tile() { return kBN; }
+
+// Reads and clears the bounded-wait timeout flags of this file's kernels.
+int sm100_bwd_timeouts() {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, sm100::g_wait_timeout, sizeof(int));
+    cudaMemcpyToSymbol(sm100::g_wait_timeout, &z, sizeof(int));
+    return v;
+}
 
 int sm100_bwd(const Params& p, int dtype, bool causal, cudaStream_t s) {
     if (dtype == NNOP_BF16)

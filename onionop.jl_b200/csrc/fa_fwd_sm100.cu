@@ -113,7 +113,10 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         n_kt = n_kt < lim ? n_kt : lim;
     }
 
+    __shared__ int s_abort;   // set by the first wait of this CTA that gives up
+    volatile int* ab = &s_abort;
     if (threadIdx.x == 0) {
+        s_abort = 0;
         mbar_init(&bars[kQFull], 1);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&bars[kKFull + s], 1);
@@ -158,7 +161,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             int issued = 0;
             for (int j = 0; j < n_kt; ++j) {
                 const int s = j % kStages;
-                if (j >= kStages && !wait(&bars[kKVEmpty + s], ((j / kStages) - 1) & 1)) break;
+                if (j >= kStages && !wait(&bars[kKVEmpty + s], ((j / kStages) - 1) & 1, ab, 1)) break;
                 issued = j + 1;
                 const int k0 = j * kBN;
                 mbar_expect_tx(&bars[kKFull + s], L::kKVBytes);
@@ -174,10 +177,10 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             }
             // Copies still in flight must land before the CTA can exit (they
             // have, unless a consumer gave up): bounded waits on the last ones.
-            wait(&bars[kQFull], 0);
+            wait(&bars[kQFull], 0, ab, 2);
             for (int j = issued - kStages < 0 ? 0 : issued - kStages; j < issued; ++j) {
-                wait(&bars[kKFull + j % kStages], (j / kStages) & 1);
-                wait(&bars[kVFull + j % kStages], (j / kStages) & 1);
+                wait(&bars[kKFull + j % kStages], (j / kStages) & 1, ab, 3);
+                wait(&bars[kVFull + j % kStages], (j / kStages) & 1, ab, 4);
             }
         }
     } else if (warp == 1) {
@@ -185,10 +188,10 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t idesc_s = idesc_f16<kBF16>(kBM, kBN, false, false);
         constexpr uint32_t idesc_o = idesc_f16<kBF16>(kBM, E, false, true);
         const uint32_t sQ = smem_u32(smem + L::kQ);
-        bool ok = n_kt > 0 && wait(&bars[kQFull], 0);
+        bool ok = n_kt > 0 && wait(&bars[kQFull], 0, ab, 5);
         auto issue_s = [&](int j) -> bool {
             const int s = j % kStages;
-            if (!wait(&bars[kKFull + s], (j / kStages) & 1)) return false;
+            if (!wait(&bars[kKFull + s], (j / kStages) & 1, ab, 6)) return false;
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t sK = smem_u32(smem + L::kK + s * L::kKVBytes);
@@ -208,8 +211,8 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int j = 0; ok && j < n_kt; ++j) {
             if (j + 1 < n_kt && !issue_s(j + 1)) break;
             const int s = j % kStages;
-            if (!wait(&bars[kPFull + (j & 1)], (j >> 1) & 1)) break;
-            if (!wait(&bars[kVFull + s], (j / kStages) & 1)) break;
+            if (!wait(&bars[kPFull + (j & 1)], (j >> 1) & 1, ab, 7)) break;
+            if (!wait(&bars[kVFull + s], (j / kStages) & 1, ab, 8)) break;
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t sV = smem_u32(smem + L::kV + s * L::kKVBytes);
@@ -229,7 +232,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (n_kt > 0) {
             if (lane == 0) umma_commit(&bars[kMmaDone]);
             __syncwarp();
-            wait(&bars[kMmaDone], 0);
+            wait(&bars[kMmaDone], 0, ab, 9);
         }
     } else if (warp < 4) {
         // ------------------------------------------------------ tile provider
@@ -245,13 +248,13 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 const int64_t k0 = (int64_t)j * kBN;
                 if (j >= 2) {
                     // my softmax is done with slot `buf` (tile j-2): tell every sender
-                    if (!wait(&bars[kTileEmpty + buf], ((j >> 1) - 1) & 1)) break;
+                    if (!wait(&bars[kTileEmpty + buf], ((j >> 1) - 1) & 1, ab, 10)) break;
                     if (tp == 0) {
                         const uint32_t eb = smem_u32(&bars[kPairEmpty + buf]);
                         for (int d = 0; d < XC; ++d) mbar_arrive_remote(mapa(eb, d));
                     }
                     // and every receiver is done with it before I overwrite it
-                    if (!wait_cluster(&bars[kPairEmpty + buf], ((j >> 1) - 1) & 1)) break;
+                    if (!wait_cluster(&bars[kPairEmpty + buf], ((j >> 1) - 1) & 1, ab, 11)) break;
                 }
                 if (tp == 0) {
                     mbar_expect_tx(&bars[kStageFull], L::kStageBytes);
@@ -267,7 +270,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     }
                     bits[buf * (kBN / 32) + tp] = w;
                 }
-                if (!wait(&bars[kStageFull], j & 1)) break;
+                if (!wait(&bars[kStageFull], j & 1, ab, 12)) break;
                 named_bar_sync(1, 64);
                 if (tp == 0) mbar_expect_tx_cluster(&bars[kTileFull + buf], kBN * kBM * 2);
                 const uint32_t full_bar = smem_u32(&bars[kTileFull + buf]);
@@ -307,7 +310,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const T* pg = PAIR ? reinterpret_cast<const T*>(p.pair) + (int64_t)b * KL * QL * p.QH + h : nullptr;
             for (int j = 0; j < n_kt; ++j) {
                 const int buf = j & 1;
-                if (j >= 2 && !wait(&bars[kTileEmpty + buf], ((j >> 1) - 1) & 1)) break;
+                if (j >= 2 && !wait(&bars[kTileEmpty + buf], ((j >> 1) - 1) & 1, ab, 13)) break;
                 const int64_t k0 = (int64_t)j * kBN;
                 if (tp < kBN / 32) {
                     uint32_t w = 0;
@@ -352,11 +355,11 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const int buf = j & 1;
             const int64_t k0 = (int64_t)j * kBN;
             if (kProvider) {
-                const bool got = XC ? wait_cluster(&bars[kTileFull + buf], (j >> 1) & 1)
-                                    : wait(&bars[kTileFull + buf], (j >> 1) & 1);
+                const bool got = XC ? wait_cluster(&bars[kTileFull + buf], (j >> 1) & 1, ab, 14)
+                                    : wait(&bars[kTileFull + buf], (j >> 1) & 1, ab, 14);
                 if (!got) { ok = false; break; }
             }
-            if (!wait(&bars[kSFull + buf], (j >> 1) & 1)) { ok = false; break; }
+            if (!wait(&bars[kSFull + buf], (j >> 1) & 1, ab, 15)) { ok = false; break; }
             tc_fence_after();
             const uint32_t tS = (buf ? tS1 : tS0) + lane_off;
             float x[kBN];
@@ -421,7 +424,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             l = l * alpha + ls;
             if (resc && j > 0 && alpha != 1.f) {
                 // O holds Σ_{<j} P·V; PV_{j-1} must be complete before rescaling.
-                if (!wait(&bars[kOStep], (j - 1) & 1)) { ok = false; break; }
+                if (!wait(&bars[kOStep], (j - 1) & 1, ab, 16)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < E / 32; ++c) {
@@ -443,7 +446,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const float m_use = (m == -INFINITY) ? 0.f : m;
             p.lse[((int64_t)b * p.QH + h) * QL + i] = m_use * 0.6931471805599453f + logf(l);
         }
-        if (n_kt > 0 && ok && wait(&bars[kOFinal], 0)) {
+        if (n_kt > 0 && ok && wait(&bars[kOFinal], 0, ab, 17)) {
             tc_fence_after();
             const float inv = 1.0f / l;
 #pragma unroll

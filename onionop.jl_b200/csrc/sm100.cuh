@@ -65,18 +65,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase of `bar` with the given parity.  Gives up after
-// about `kWaitCycles` SM cycles (~1 s), records the timeout in g_wait_timeout
-// and returns false; the caller then stops its role loop.
+// about `kWaitCycles` SM cycles (~1 s): it then sets the CTA's shared abort
+// flag (`abort`), records bit `site` in g_wait_timeout and returns false; the
+// caller stops its role loop.  Every later wait of the CTA sees the abort flag
+// and returns false at once, so a CTA that gave up leaves within ~1 s instead
+// of timing out wait after wait.
 constexpr long long kWaitCycles = 2000000000LL;
-__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool wait_give_up(volatile int* abort, int site) {
+    if (abort) *abort = 1;
+    atomicOr(&g_wait_timeout, 1 << (site & 31));
+    return false;
+}
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, volatile int* abort = nullptr, int site = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (clock64() - t0 > kWaitCycles) {
-            atomicExch(&g_wait_timeout, 1);
-            return false;
-        }
+        if (abort && *abort) return false;
+        if (clock64() - t0 > kWaitCycles) return wait_give_up(abort, site);
     }
 }
 
@@ -93,15 +99,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ bool wait_cluster(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort = nullptr,
+                                             int site = 0) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (clock64() - t0 > kWaitCycles) {
-            atomicExch(&g_wait_timeout, 1);
-            return false;
-        }
+        if (abort && *abort) return false;
+        if (clock64() - t0 > kWaitCycles) return wait_give_up(abort, site);
     }
 }
 

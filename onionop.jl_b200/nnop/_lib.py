@@ -28,6 +28,7 @@ SIGNATURES = {
     "nnop_abi_version": (_int, []),
     "nnop_last_error": (C.c_char_p, []),
     "nnop_status_string": (C.c_char_p, [_int]),
+    "nnop_device_wait_timeouts": (_int, []),
     "nnop_flash_attention_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "nnop_flash_attention_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
