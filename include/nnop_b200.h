@@ -91,18 +91,29 @@ int nnop_device_wait_timeouts(void);
  * causal && j > i or kpad_mask[b][j] == 0; scale = dtype(1/sqrt(E)).
  * Checks (src/attention.jl:185-188): E must be a power of two (16..128 here),
  * QH % KH == 0.  dtype: F32, F16, BF16.
+ *   workspace: with a pair bias, >= nnop_flash_attention_fwd_workspace_size(...)
+ *   bytes, 256-byte aligned, holding per-head copies of the pair tiles for the
+ *   tensor-core kernel; NULL (or too small) selects the slower kernel that
+ *   reads the head-innermost pair directly.  Unused without a pair bias.
  */
 int nnop_flash_attention_fwd(const void* q, const void* k, const void* v,
                              const void* pair, const uint8_t* kpad_mask,
                              void* o, float* lse,
+                             void* workspace, size_t workspace_bytes,
                              int64_t E, int64_t QL, int64_t KL,
                              int64_t QH, int64_t KH, int64_t B,
                              int causal, int dtype, void* stream);
 
-/* Bytes of workspace nnop_flash_attention_bwd needs for these dimensions. */
+/* Bytes of workspace nnop_flash_attention_fwd can use (0 = none needed). */
+size_t nnop_flash_attention_fwd_workspace_size(int64_t E, int64_t QL, int64_t KL,
+                                               int64_t QH, int64_t KH, int64_t B,
+                                               int has_pair, int dtype);
+
+/* Bytes of workspace nnop_flash_attention_bwd needs for these dimensions
+ * (has_pair: a pair bias / dpair will be passed). */
 size_t nnop_flash_attention_bwd_workspace_size(int64_t E, int64_t QL, int64_t KL,
                                                int64_t QH, int64_t KH, int64_t B,
-                                               int dtype);
+                                               int has_pair, int dtype);
 
 /*
  * Backward.  Replaces `∇flash_attention` (src/attention_bwd.jl:213-303) with

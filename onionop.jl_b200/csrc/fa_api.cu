@@ -4,6 +4,7 @@
 #include "fa_common.cuh"
 
 #include <cstdlib>
+#include <type_traits>
 
 namespace nnop {
 namespace fa {
@@ -13,14 +14,26 @@ int mma_tile();
 int simt_fwd(const Params& p, bool causal, cudaStream_t s);
 int simt_bwd(const Params& p, bool causal, cudaStream_t s);
 int simt_tile();
-bool sm100_fwd_supported(const Params& p, int dtype);
-int sm100_fwd(const Params& p, int dtype, bool causal, cudaStream_t s);
+bool sm100_fwd_supported(const Params& p, int dtype, bool have_pair_tiles);
+int sm100_fwd(const Params& p, const void* pair_tiles, int dtype, bool causal, cudaStream_t s);
 bool sm100_bwd_supported(const Params& p, int dtype);
-int sm100_bwd(const Params& p, int dtype, bool causal, cudaStream_t s);
+int sm100_bwd(const Params& p, const void* pair_tiles, void* ds_tiles, int dtype, bool causal, cudaStream_t s);
 int sm100_bwd_tile();
 int sm100_fwd_timeouts();
 int sm100_bwd_timeouts();
 }  // namespace fa
+
+namespace fa_host {
+size_t pair_tiles_bytes(int64_t QL, int64_t KL, int64_t H, int64_t B);
+template <typename T>
+int launch_pair_tiles_fwd(const T* pair, T* out, int64_t QL, int64_t KL, int H, int B, bool causal, cudaStream_t s);
+template <typename T>
+int launch_pair_tiles_bwd(const T* pair, T* out, const int* kv_len, int64_t QL, int64_t KL, int H, int B, bool causal,
+                          cudaStream_t s);
+template <typename T>
+int launch_dpair_from_tiles(const T* tiles, T* dpair, const int* kv_len, int64_t QL, int64_t KL, int H, int B,
+                            bool causal, cudaStream_t s);
+}  // namespace fa_host
 
 namespace {
 
@@ -53,14 +66,23 @@ int check_dims(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_
     return NNOP_OK;
 }
 
+// The tcgen05 kernels take the pair bias as per-head tiles (pair_tiles.cu):
+// bf16/f16, E = 64, at most 64 heads (the re-layout stages [8][128][H] blocks).
+bool pair_tiles_path(int64_t E, int64_t QH, int dtype) {
+    return !force_mma() && (dtype == NNOP_BF16 || dtype == NNOP_F16) && E == 64 && QH <= 64;
+}
+
 struct BwdWorkspace {
     int* kv_len;
     float* delta;
     float* dq_acc;
+    void* pair_tiles;   // tcgen05 path with a pair bias: per-head pair tiles
+    void* ds_tiles;     // ... and the per-head dS tiles
     size_t bytes;
 };
 
-BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t QH, int64_t B, int dtype) {
+BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t B, bool has_pair,
+                        int dtype) {
     BwdWorkspace w{};
     size_t off = 0;
     char* p = static_cast<char*>(base);
@@ -74,8 +96,50 @@ BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t QH, int64_t B
     } else {
         w.dq_acc = nullptr;
     }
+    w.pair_tiles = w.ds_tiles = nullptr;
+    if (has_pair && pair_tiles_path(E, QH, dtype)) {
+        const size_t tb = align256(fa_host::pair_tiles_bytes(QL, KL, QH, B));
+        w.pair_tiles = p ? p + off : nullptr;
+        off += tb;
+        w.ds_tiles = p ? p + off : nullptr;
+        off += tb;
+    }
     w.bytes = off;
     return w;
+}
+
+// f16/bf16 backward: delta, dq accumulator, the tcgen05 (or mma.sync) kernel,
+// dq conversion, and dpair (from the per-head dS tiles, or the zero fill of the
+// tiles the mma.sync kernel does not visit).
+template <typename T>
+int bwd_16bit(fa::Params& p, const BwdWorkspace& ws, int64_t rows, bool causal, int dtype, cudaStream_t s) {
+    const int64_t E = p.E, QL = p.QL, KL = p.KL;
+    const float sc = (float)(1.0 / sqrt((double)E));
+    p.scale = std::is_same<T, __nv_bfloat16>::value ? __bfloat162float(__float2bfloat16_rn(sc))
+                                                    : __half2float(__float2half_rn(sc));
+    if (cudaMemsetAsync(ws.dq_acc, 0, (size_t)rows * E * sizeof(float), s) != cudaSuccess)
+        return fail(NNOP_ERR_CUDA, "flash_attention_bwd: memset failed");
+    p.dq_acc = ws.dq_acc;
+    const bool tc = !force_mma() && fa::sm100_bwd_supported(p, dtype) && (p.pair == nullptr || ws.pair_tiles);
+    int st = fa_host::launch_preprocess<T>((const T*)p.dO, (const T*)p.o, ws.delta, rows, (int)E, s);
+    if (st) return st;
+    if (tc) {
+        if (p.pair) {
+            st = fa_host::launch_pair_tiles_bwd<T>((const T*)p.pair, (T*)ws.pair_tiles, p.kv_len, QL, KL, p.QH, p.B,
+                                                   causal, s);
+            if (st) return st;
+        }
+        st = fa::sm100_bwd(p, ws.pair_tiles, ws.ds_tiles, dtype, causal, s);
+    } else {
+        st = fa::mma_bwd<T>(p, causal, s);
+    }
+    if (st) return st;
+    st = fa_host::launch_convert<T>(ws.dq_acc, (T*)p.dq, rows * E, s);
+    if (st || !p.pair) return st;
+    if (tc)
+        return fa_host::launch_dpair_from_tiles<T>((const T*)ws.ds_tiles, (T*)p.dpair, p.kv_len, QL, KL, p.QH, p.B,
+                                                   causal, s);
+    return fa_host::launch_dpair_fill<T>((T*)p.dpair, p.kv_len, QL, KL, p.QH, p.B, fa::mma_tile(), causal, s);
 }
 
 }  // namespace
@@ -91,9 +155,18 @@ int nnop_device_wait_timeouts(void) {
     return (f & 0xffff) | ((b & 0x7fff) << 16);
 }
 
+size_t nnop_flash_attention_fwd_workspace_size(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_t B,
+                                               int has_pair, int dtype) {
+    (void)KH;
+    if (E <= 0 || QL < 0 || KL < 0 || QH <= 0 || B < 0) return 0;
+    if (!has_pair || !pair_tiles_path(E, QH, dtype)) return 0;
+    return align256(fa_host::pair_tiles_bytes(QL, KL, QH, B));
+}
+
 int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const void* pair,
-                             const uint8_t* kpad_mask, void* o, float* lse, int64_t E, int64_t QL, int64_t KL,
-                             int64_t QH, int64_t KH, int64_t B, int causal, int dtype, void* stream) {
+                             const uint8_t* kpad_mask, void* o, float* lse, void* workspace, size_t workspace_bytes,
+                             int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_t B, int causal,
+                             int dtype, void* stream) {
     int st = check_dims(E, QL, KL, QH, KH, B, dtype);
     if (st) return st;
     if (QL == 0 || B == 0) return NNOP_OK;
@@ -110,22 +183,38 @@ int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const 
             p.scale = (float)(1.0 / sqrt((double)E));
             return fa::simt_fwd(p, causal != 0, s);
         case NNOP_F16:
-            p.scale = __half2float(__float2half_rn((float)(1.0 / sqrt((double)E))));
-            if (!force_mma() && fa::sm100_fwd_supported(p, dtype)) return fa::sm100_fwd(p, dtype, causal != 0, s);
-            return fa::mma_fwd<__half>(p, causal != 0, s);
-        case NNOP_BF16:
-            p.scale = __bfloat162float(__float2bfloat16_rn((float)(1.0 / sqrt((double)E))));
-            if (!force_mma() && fa::sm100_fwd_supported(p, dtype)) return fa::sm100_fwd(p, dtype, causal != 0, s);
-            return fa::mma_fwd<__nv_bfloat16>(p, causal != 0, s);
+        case NNOP_BF16: {
+            const bool bf = dtype == NNOP_BF16;
+            const float sc = (float)(1.0 / sqrt((double)E));
+            p.scale = bf ? __bfloat162float(__float2bfloat16_rn(sc)) : __half2float(__float2half_rn(sc));
+            // The pair bias reaches the tcgen05 kernel as per-head tiles written
+            // into the workspace; without (enough) workspace the mma.sync
+            // kernel, which reads the pair directly, runs instead.
+            const size_t need = nnop_flash_attention_fwd_workspace_size(E, QL, KL, QH, KH, B, pair != nullptr, dtype);
+            const bool tiles = pair != nullptr && need > 0 && workspace != nullptr && workspace_bytes >= need &&
+                               (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0;
+            if (!force_mma() && fa::sm100_fwd_supported(p, dtype, tiles)) {
+                if (tiles) {
+                    st = bf ? fa_host::launch_pair_tiles_fwd<__nv_bfloat16>((const __nv_bfloat16*)pair,
+                                                                             (__nv_bfloat16*)workspace, QL, KL, (int)QH,
+                                                                             (int)B, causal != 0, s)
+                            : fa_host::launch_pair_tiles_fwd<__half>((const __half*)pair, (__half*)workspace, QL, KL,
+                                                                     (int)QH, (int)B, causal != 0, s);
+                    if (st) return st;
+                }
+                return fa::sm100_fwd(p, workspace, dtype, causal != 0, s);
+            }
+            return bf ? fa::mma_fwd<__nv_bfloat16>(p, causal != 0, s) : fa::mma_fwd<__half>(p, causal != 0, s);
+        }
     }
     return fail(NNOP_ERR_DTYPE, "flash_attention_fwd: unsupported dtype");
 }
 
 size_t nnop_flash_attention_bwd_workspace_size(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_t B,
-                                               int dtype) {
-    (void)KL; (void)KH;
-    if (E <= 0 || QL < 0 || QH <= 0 || B < 0) return 0;
-    return bwd_layout(nullptr, E, QL, QH, B, dtype).bytes;
+                                               int has_pair, int dtype) {
+    (void)KH;
+    if (E <= 0 || QL < 0 || KL < 0 || QH <= 0 || B < 0) return 0;
+    return bwd_layout(nullptr, E, QL, KL, QH, B, has_pair != 0, dtype).bytes;
 }
 
 int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, const void* q, const void* k,
@@ -152,7 +241,7 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, co
     if (!aligned16(dO) || !aligned16(o) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dq) ||
         !aligned16(dk) || !aligned16(dv))
         return fail(NNOP_ERR_ALIGN, "flash_attention_bwd: dense tensors must be 16-byte aligned");
-    BwdWorkspace ws = bwd_layout(workspace, E, QL, QH, B, dtype);
+    BwdWorkspace ws = bwd_layout(workspace, E, QL, KL, QH, B, pair != nullptr, dtype);
     if (!workspace || workspace_bytes < ws.bytes)
         return fail(NNOP_ERR_WORKSPACE, "flash_attention_bwd: workspace too small (need " + std::to_string(ws.bytes) +
                                             " bytes)");
@@ -189,32 +278,9 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, co
             return st;
         }
         case NNOP_F16:
-        case NNOP_BF16: {
-            if (cudaMemsetAsync(ws.dq_acc, 0, (size_t)rows * E * sizeof(float), s) != cudaSuccess)
-                return fail(NNOP_ERR_CUDA, "flash_attention_bwd: memset failed");
-            p.dq_acc = ws.dq_acc;
-            const bool tc = !force_mma() && fa::sm100_bwd_supported(p, dtype);
-            const int tile = tc ? fa::sm100_bwd_tile() : fa::mma_tile();
-            if (dtype == NNOP_F16) {
-                p.scale = __half2float(__float2half_rn((float)(1.0 / sqrt((double)E))));
-                st = fa_host::launch_preprocess<__half>((const __half*)dO, (const __half*)o, ws.delta, rows, (int)E, s);
-                if (!st) st = tc ? fa::sm100_bwd(p, dtype, c, s) : fa::mma_bwd<__half>(p, c, s);
-                if (!st) st = fa_host::launch_convert<__half>(ws.dq_acc, (__half*)dq, rows * E, s);
-                if (!st && pair)
-                    st = fa_host::launch_dpair_fill<__half>((__half*)dpair, p.kv_len, QL, KL, (int)QH, (int)B,
-                                                            tile, c, s);
-            } else {
-                p.scale = __bfloat162float(__float2bfloat16_rn((float)(1.0 / sqrt((double)E))));
-                st = fa_host::launch_preprocess<__nv_bfloat16>((const __nv_bfloat16*)dO, (const __nv_bfloat16*)o,
-                                                               ws.delta, rows, (int)E, s);
-                if (!st) st = tc ? fa::sm100_bwd(p, dtype, c, s) : fa::mma_bwd<__nv_bfloat16>(p, c, s);
-                if (!st) st = fa_host::launch_convert<__nv_bfloat16>(ws.dq_acc, (__nv_bfloat16*)dq, rows * E, s);
-                if (!st && pair)
-                    st = fa_host::launch_dpair_fill<__nv_bfloat16>((__nv_bfloat16*)dpair, p.kv_len, QL, KL, (int)QH,
-                                                                   (int)B, tile, c, s);
-            }
-            return st;
-        }
+            return bwd_16bit<__half>(p, ws, rows, c, dtype, s);
+        case NNOP_BF16:
+            return bwd_16bit<__nv_bfloat16>(p, ws, rows, c, dtype, s);
     }
     return fail(NNOP_ERR_DTYPE, "flash_attention_bwd: unsupported dtype");
 }

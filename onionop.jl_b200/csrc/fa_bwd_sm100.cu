@@ -14,12 +14,16 @@
 //   dK += dSᵀ·Q_i   (dSᵀ from TMEM)                     UMMA ts
 //   dQ_i = dS·K     (dS from shared memory, MN-major)   UMMA ss
 //   dq_acc[i] += scale·dQ_i  (fp32 vector reductions, red.global.add.v4.f32)
-//   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale).
+//   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
+//                 written per head as dS tiles, see pair_tiles.cu.
 // Warp roles (512 threads):
 //   warp 0      TMA producer (K, V once; Q_i, dO_i into a 2-stage ring)
 //   warp 1      MMA issuer (one lane)
-//   warps 2-3   tile provider: lse_i (log2 units), δ_i and the pair tile
-//               rearranged to [query/8][key][8]
+//   warps 2-3   tile provider: lse_i (log2 units) and δ_i
+//   (the pair tile of (query tile, key tile, head) is a TMA box of the per-head
+//   copy pair_tiles_bwd() writes, [B][H][QL/8][KL][8], issued by warp 0; dS
+//   goes out as 16-byte rows in the same layout and dpair_from_tiles() turns
+//   it into dpair)
 //   warps 4-11  elementwise: two warpgroups on the same 128 TMEM lanes
 //               (one key per lane), query columns [0,64) and [64,128)
 //   warps 12-15 dQ: TMEM dQ rows -> fp32 reductions into the accumulator
@@ -30,6 +34,7 @@
 #include <cuda.h>
 
 #include <cstdlib>
+#include <cstring>
 
 #include "fa_common.cuh"
 #include "fa_sm100.cuh"
@@ -57,7 +62,9 @@ enum Bar {
     kTileFull = 9,    // +buffer: provider -> elementwise (64 arrivals)
     kTileEmpty = 11,  // +buffer: elementwise -> provider (256 arrivals)
     kFinal = 13,      // every MMA retired
-    kNumBars = 14
+    kPairFull = 14,   // +buffer: pair tile landed (TMA)
+    kPairEmpty = 16,  // +buffer: elementwise done with it (256 arrivals)
+    kNumBars = 18
 };
 
 struct Lay {
@@ -84,12 +91,19 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
+// Warp-uniform bounded wait: true only if every lane saw the phase complete
+// (guards warp-wide tcgen05.ld/st, which must not run divergent).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* ab, int site) {
+    const bool ok = wait(bar, parity, ab, site);
+    return __all_sync(0xffffffffu, ok);
+}
 
 template <typename T, bool CAUSAL, bool PAIR, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const Params p) {
+                    const __grid_constant__ CUtensorMap tm_pair, const Params p, uint16_t* __restrict__ ds_tiles,
+                    int64_t qlp, int64_t klp) {
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -119,6 +133,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             mbar_init(&bars[kQEmpty + s], 1);
             mbar_init(&bars[kTileFull + s], 64);
             mbar_init(&bars[kTileEmpty + s], 256);
+            mbar_init(&bars[kPairFull + s], 1);
+            mbar_init(&bars[kPairEmpty + s], 256);
         }
         mbar_init(&bars[kSFull], 1);
         mbar_init(&bars[kPFull], 256);
@@ -144,6 +160,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             tma_prefetch(&tm_k);
             tma_prefetch(&tm_v);
             tma_prefetch(&tm_do);
+            if (PAIR) tma_prefetch(&tm_pair);
             const int bh_k = b * p.KH + kvh;
             mbar_expect_tx(&bars[kKVFull], 2 * Lay::kTile);
             tma_load_3d(smem + Lay::kK, &tm_k, &bars[kKVFull], 0, (int)k0, bh_k);
@@ -152,17 +169,25 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             for (int st = 0; st < steps; ++st) {
                 const int s = st & 1;
                 if (st >= 2 && !wait(&bars[kQEmpty + s], ((st >> 1) - 1) & 1, ab, 1)) break;
+                if (PAIR && st >= 2 && !wait(&bars[kPairEmpty + s], ((st >> 1) - 1) & 1, ab, 14)) break;
                 issued = st + 1;
                 const int h = kvh * p.n_rep + st / nq;
                 const int q0 = (qt0 + st % nq) * kBM;
                 mbar_expect_tx(&bars[kQFull + s], 2 * Lay::kTile);
                 tma_load_3d(smem + Lay::kQ + s * Lay::kTile, &tm_q, &bars[kQFull + s], 0, q0, b * QH + h);
                 tma_load_3d(smem + Lay::kDO + s * Lay::kTile, &tm_do, &bars[kQFull + s], 0, q0, b * QH + h);
+                if (PAIR) {
+                    mbar_expect_tx(&bars[kPairFull + s], Lay::kPairBytes);
+                    tma_load_3d(smem + Lay::kPair + s * Lay::kPairBytes, &tm_pair, &bars[kPairFull + s], 0, (int)k0,
+                                (int)(((int64_t)b * QH + h) * (qlp / 8) + q0 / 8));
+                }
             }
             // copies in flight land before the CTA leaves (bounded waits)
             wait(&bars[kKVFull], 0, ab, 2);
-            for (int st = issued - 2 < 0 ? 0 : issued - 2; st < issued; ++st)
+            for (int st = issued - 2 < 0 ? 0 : issued - 2; st < issued; ++st) {
                 wait(&bars[kQFull + (st & 1)], (st >> 1) & 1, ab, 3);
+                if (PAIR) wait(&bars[kPairFull + (st & 1)], (st >> 1) & 1, ab, 15);
+            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -171,10 +196,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t id_q = idesc_f16<kBF16>(128, 64, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
         const uint32_t sDS = smem_u32(smem + Lay::kDS);
-        bool ok = steps > 0 && wait(&bars[kKVFull], 0, ab, 4);
+        bool ok = steps > 0 && wait_warp(&bars[kKVFull], 0, ab, 4);
         for (int st = 0; ok && st < steps; ++st) {
             const int s = st & 1;
-            if (!wait(&bars[kQFull + s], (st >> 1) & 1, ab, 5)) break;
+            if (!wait_warp(&bars[kQFull + s], (st >> 1) & 1, ab, 5)) break;
             tc_fence_after();
             const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile);
             const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile);
@@ -187,7 +212,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 umma_commit(&bars[kSFull]);
             }
             __syncwarp();
-            if (!wait(&bars[kPFull], st & 1, ab, 6)) break;
+            if (!wait_warp(&bars[kPFull], st & 1, ab, 6)) break;
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
@@ -201,7 +226,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 umma_commit(&bars[kQEmpty + s]);
             }
             __syncwarp();
-            if (st > 0 && !wait(&bars[kDQEmpty], (st - 1) & 1, ab, 7)) break;
+            if (st > 0 && !wait_warp(&bars[kDQEmpty], (st - 1) & 1, ab, 7)) break;
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
@@ -230,25 +255,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 sLse[buf * kBM + t] = i < QL ? p.lse[ro + i] * kLog2e : 0.f;
                 sDel[buf * kBM + t] = i < QL ? p.delta[ro + i] : 0.f;
             }
-            if (PAIR) {
-                const T* pg = reinterpret_cast<const T*>(p.pair) + (int64_t)b * KL * QL * QH + h;
-                uint8_t* dst = smem + Lay::kPair + buf * Lay::kPairBytes;
-#pragma unroll 1
-                for (int jj = 0; jj < kBN / 64; ++jj) {
-                    const int jr = tp + jj * 64;
-                    const int64_t key = k0 + jr;
-#pragma unroll 2
-                    for (int g = 0; g < kBM / 8; ++g) {
-                        T v8[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const int64_t i = q0 + g * 8 + e;
-                            v8[e] = (i < QL && key < KL) ? pg[(key * QL + i) * QH] : from_f<T>(0.f);
-                        }
-                        *reinterpret_cast<uint4*>(dst + ((g * kBN + jr) * 8) * 2) = *reinterpret_cast<uint4*>(v8);
-                    }
-                }
-            }
             mbar_arrive(&bars[kTileFull + buf]);
         }
     } else if (warp < 12) {
@@ -265,10 +271,12 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const int buf = st & 1;
             const int h = kvh * p.n_rep + st / nq;
             const int64_t q0 = (int64_t)(qt0 + st % nq) * kBM;
-            if (!wait(&bars[kTileFull + buf], (st >> 1) & 1, ab, 10)) break;
-            if (!wait(&bars[kSFull], st & 1, ab, 11)) break;
+            if (!wait_warp(&bars[kTileFull + buf], (st >> 1) & 1, ab, 10)) break;
+            if (PAIR && !wait_warp(&bars[kPairFull + buf], (st >> 1) & 1, ab, 16)) break;
+            if (!wait_warp(&bars[kSFull], st & 1, ab, 11)) break;
             tc_fence_after();
-            uint16_t* dpg = PAIR ? reinterpret_cast<uint16_t*>(p.dpair) + (int64_t)b * KL * QL * QH + h : nullptr;
+            // dS tile rows of this key: [b][h][query/8][key][8]
+            uint16_t* dst_row = PAIR ? ds_tiles + ((((int64_t)b * QH + h) * (qlp / 8) + q0 / 8) * klp + j) * 8 : nullptr;
 #pragma unroll 1
             for (int cc = 0; cc < 4; ++cc) {
                 const int col = c0 + cc * 16;
@@ -319,25 +327,22 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     uint4* dst = reinterpret_cast<uint4*>(sDS + half * (128 * 128) + jr * 128 + ((chunk ^ (jr & 7)) << 4));
                     *dst = make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]);
                 }
-                if (PAIR && j < KL) {
+                if (PAIR) {
 #pragma unroll
-                    for (int t = 0; t < 16; ++t) {
-                        const int64_t i = q0 + col + t;
-                        if (i < QL) {
-                            const uint32_t w = dk[t >> 1];
-                            dpg[(j * QL + i) * QH] = (t & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xffff);
-                        }
-                    }
+                    for (int v = 0; v < 2; ++v)
+                        __stcs(reinterpret_cast<uint4*>(dst_row + (int64_t)((col >> 3) + v) * klp * 8),
+                               make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]));
                 }
             }
             mbar_arrive(&bars[kTileEmpty + buf]);
+            if (PAIR) mbar_arrive(&bars[kPairEmpty + buf]);
             tmem_st_wait();
             fence_proxy_async_smem();   // dS smem writes -> tensor-core (async proxy) reads
             tc_fence_before();
             mbar_arrive(&bars[kPFull]);
         }
         // epilogue: dK (warpgroup 0) and dV (warpgroup 1) rows of this CTA's keys
-        if (wait(&bars[kFinal], 0, ab, 12)) {
+        if (wait_warp(&bars[kFinal], 0, ab, 12)) {
             tc_fence_after();
             const bool is_dk = c0 == 0;
             const uint32_t src = (is_dk ? tDK : tDV) + lane_off;
@@ -367,7 +372,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int st = 0; st < steps; ++st) {
             const int h = kvh * p.n_rep + st / nq;
             const int64_t i = (int64_t)(qt0 + st % nq) * kBM + r;
-            if (!wait(&bars[kDQFull], st & 1, ab, 13)) break;
+            if (!wait_warp(&bars[kDQFull], st & 1, ab, 13)) break;
             tc_fence_after();
             float* dq = p.dq_acc + (((int64_t)b * QH + h) * QL + i) * kE;
 #pragma unroll
@@ -395,30 +400,48 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
 }
 
+// 3-D map over the per-head backward pair tiles [B·H·QLp/8][KLp][8], box
+// (8, 128, 16): one (128-key, 128-query) tile as [query/8][key][8].
+bool make_pair_tiles_map_bwd(CUtensorMap* m, const void* base, int64_t klp, int64_t rows, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {8, (cuuint64_t)klp, (cuuint64_t)rows};
+    cuuint64_t strides[2] = {16, (cuuint64_t)klp * 16};
+    cuuint32_t box[3] = {8, (cuuint32_t)kBN, (cuuint32_t)(kBM / 8)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 template <typename T, bool CAUSAL, bool PAIR, bool MASK>
-int launch(const Params& p, cudaStream_t s) {
+int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t s) {
     constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-    CUtensorMap tq, tk, tv, tdo;
+    const int64_t qlp = (p.QL + 127) / 128 * 128, klp = (p.KL + 127) / 128 * 128;
+    CUtensorMap tq, tk, tv, tdo, tp;
+    memset(&tp, 0, sizeof(tp));
     if (!make_map(&tq, p.q, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
-        !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16))
+        !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
+        (PAIR && !make_pair_tiles_map_bwd(&tp, pair_tiles, klp, (int64_t)p.B * p.QH * (qlp / 8), bf16)))
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_bwd_sm100_kernel<T, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cannot set shared memory size");
     dim3 grid((unsigned)((p.KL + kBN - 1) / kBN), p.KH, p.B);
-    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tdo, p);
+    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tdo, tp, p, static_cast<uint16_t*>(ds_tiles), qlp, klp);
     return check_launch("flash_attention_bwd (sm100)");
 }
 
 template <typename T, bool CAUSAL>
-int dispatch_flags(const Params& p, cudaStream_t s) {
+int dispatch_flags(const Params& p, const void* pt, void* dt, cudaStream_t s) {
     const bool pair = p.pair != nullptr, mask = p.kmask != nullptr;
-    if (pair && mask) return launch<T, CAUSAL, true, true>(p, s);
-    if (pair) return launch<T, CAUSAL, true, false>(p, s);
-    if (mask) return launch<T, CAUSAL, false, true>(p, s);
-    return launch<T, CAUSAL, false, false>(p, s);
+    if (pair && mask) return launch<T, CAUSAL, true, true>(p, pt, dt, s);
+    if (pair) return launch<T, CAUSAL, true, false>(p, pt, dt, s);
+    if (mask) return launch<T, CAUSAL, false, true>(p, pt, dt, s);
+    return launch<T, CAUSAL, false, false>(p, pt, dt, s);
 }
 
 }  // namespace
@@ -437,10 +460,12 @@ int sm100_bwd_timeouts() {
     return v;
 }
 
-int sm100_bwd(const Params& p, int dtype, bool causal, cudaStream_t s) {
+int sm100_bwd(const Params& p, const void* pair_tiles, void* ds_tiles, int dtype, bool causal, cudaStream_t s) {
     if (dtype == NNOP_BF16)
-        return causal ? dispatch_flags<__nv_bfloat16, true>(p, s) : dispatch_flags<__nv_bfloat16, false>(p, s);
-    return causal ? dispatch_flags<__half, true>(p, s) : dispatch_flags<__half, false>(p, s);
+        return causal ? dispatch_flags<__nv_bfloat16, true>(p, pair_tiles, ds_tiles, s)
+                      : dispatch_flags<__nv_bfloat16, false>(p, pair_tiles, ds_tiles, s);
+    return causal ? dispatch_flags<__half, true>(p, pair_tiles, ds_tiles, s)
+                  : dispatch_flags<__half, false>(p, pair_tiles, ds_tiles, s);
 }
 
 }  // namespace fa

@@ -119,9 +119,12 @@ def _flash_attention(q, k, v, pair=None, *, causal: bool, kpad_mask=None):
     m = _mask_u8(kpad_mask)
     o = torch.empty_like(q)
     lse = torch.empty((B, QH, QL), dtype=torch.float32, device=dev)
+    dt = _dtype_id(q)
+    ws_bytes = lib.nnop_flash_attention_fwd_workspace_size(E, QL, KL, QH, KH, B, int(pair is not None), dt)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     check(lib.nnop_flash_attention_fwd(
-        _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m), _ptr(o), _ptr(lse),
-        E, QL, KL, QH, KH, B, int(bool(causal)), _dtype_id(q), _stream(dev)))
+        _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m), _ptr(o), _ptr(lse), _ptr(ws), ws_bytes,
+        E, QL, KL, QH, KH, B, int(bool(causal)), dt, _stream(dev)))
     return o, lse
 
 
@@ -138,7 +141,7 @@ def grad_flash_attention(do, o, lse, q, k, v, pair=None, *, causal: bool, kpad_m
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dpair = torch.empty_like(pair) if pair is not None else None
     dt = _dtype_id(q)
-    ws_bytes = lib.nnop_flash_attention_bwd_workspace_size(E, QL, KL, QH, KH, B, dt)
+    ws_bytes = lib.nnop_flash_attention_bwd_workspace_size(E, QL, KL, QH, KH, B, int(pair is not None), dt)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     check(lib.nnop_flash_attention_bwd(
         _ptr(do), _ptr(o), _ptr(lse), _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m),

@@ -29,9 +29,10 @@ SIGNATURES = {
     "nnop_last_error": (C.c_char_p, []),
     "nnop_status_string": (C.c_char_p, [_int]),
     "nnop_device_wait_timeouts": (_int, []),
-    "nnop_flash_attention_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp,
+    "nnop_flash_attention_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                         _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
-    "nnop_flash_attention_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
+    "nnop_flash_attention_fwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int, _int]),
+    "nnop_flash_attention_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int, _int]),
     "nnop_flash_attention_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _vp, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "nnop_online_softmax_fwd": (_int, [_vp, _vp, _i64, _i64, _int, _vp]),

@@ -51,8 +51,8 @@ def test_abi_version_and_status_strings():
 
 def _fwd(lib, E=64, QL=8, KL=8, QH=2, KH=2, B=1, dtype=2):
     dummy = C.c_void_p(256)   # never dereferenced: validation fails first
-    return lib.nnop_flash_attention_fwd(dummy, dummy, dummy, None, None, dummy, dummy, E, QL, KL, QH, KH, B, 0,
-                                        dtype, None)
+    return lib.nnop_flash_attention_fwd(dummy, dummy, dummy, None, None, dummy, dummy, None, 0, E, QL, KL, QH, KH, B,
+                                        0, dtype, None)
 
 
 def test_shape_errors_before_launch():
@@ -81,9 +81,14 @@ def test_norm_rope_errors_before_launch():
 
 def test_workspace_sizes():
     from nnop._lib import lib
-    ws = lib.nnop_flash_attention_bwd_workspace_size(64, 4096, 4096, 16, 16, 8, 2)
+    ws = lib.nnop_flash_attention_bwd_workspace_size(64, 4096, 4096, 16, 16, 8, 0, 2)
     assert ws >= 8 * 16 * 4096 * 64 * 4 + 8 * 16 * 4096 * 4
-    assert lib.nnop_flash_attention_bwd_workspace_size(64, 4096, 4096, 16, 16, 8, 0) < ws
+    assert lib.nnop_flash_attention_bwd_workspace_size(64, 4096, 4096, 16, 16, 8, 0, 0) < ws
+    tiles = 8 * 16 * 4096 * 4096 * 2
+    assert lib.nnop_flash_attention_bwd_workspace_size(64, 4096, 4096, 16, 16, 8, 1, 2) >= ws + 2 * tiles
+    assert lib.nnop_flash_attention_fwd_workspace_size(64, 4096, 4096, 16, 16, 8, 1, 2) >= tiles
+    assert lib.nnop_flash_attention_fwd_workspace_size(64, 4096, 4096, 16, 16, 8, 0, 2) == 0
+    assert lib.nnop_flash_attention_fwd_workspace_size(64, 4096, 4096, 16, 16, 8, 1, 0) == 0
     assert lib.nnop_rms_norm_bwd_workspace_size(4096, 65536) >= 4096 * 4
     assert lib.nnop_layer_norm_bwd_workspace_size(4096, 3) == 3 * 2 * 4096 * 4
 
