@@ -289,7 +289,7 @@ def run_ours(args):
     bwd_bytes = cfg_bytes(B, H, L, E, causal)[1]
     achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
     roofline = {
-        "kernel": "flash_attention_bwd call (fa_bwd_mma_kernel + preprocess, dq convert, dpair fill)",
+        "kernel": "flash_attention_bwd call (fa_bwd_sm100_kernel + preprocess, pair_tiles_bwd, dq convert, dpair_from_tiles)",
         "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
         "peak_source": f"{src} hbm_gbs", "traffic": None,
         "algorithmic_bytes_per_launch": bwd_bytes, "launch_ms": bwd_ms,
@@ -313,7 +313,8 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (pair 4.29 GB per GPU)"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
-            "gpu_launches": K * 5,
+            # per step: pair_tiles_fwd, fa_fwd; preprocess, pair_tiles_bwd, fa_bwd, dq convert, dpair_from_tiles
+            "gpu_launches": K * 7,
             "roofline": roofline,
             "clocks": clk,
         }
