@@ -59,50 +59,93 @@ def peaks():
 
 # --------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled every few ms through NVML
+    (read-only queries) in a background thread while the timed region runs;
+    nvidia-smi at its 200 ms minimum period as the fallback."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, uuid: str | None):
-        self.uuid = uuid
-        self.proc = None
-        self.path = None
+    def __init__(self, uuid: str | None, index: int = 0, period_s: float = 0.005):
+        self.uuid, self.index, self.period = uuid, index, period_s
+        self.rows, self.thread, self.stop_flag, self.nvml = [], None, False, None
+        self.smi = None
 
     def start(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            try:
+                h = nv.nvmlDeviceGetHandleByUUID(("GPU-" + self.uuid) if self.uuid else "")
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.nvml = (nv, h)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def run():
+                while not self.stop_flag:
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                        self.rows.append((sm, rs))
+                    except Exception:
+                        pass
+                    time.sleep(self.period)
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 2.0:
+                time.sleep(0.001)
+        except Exception:
+            self.nvml = None
+            self._start_smi()
+
+    def _start_smi(self):
+        fields = ("uuid,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+            self.smi = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.5)
         except Exception:
-            self.proc = None
+            self.smi = None
 
     def stop(self):
-        if self.proc is None:
+        if self.nvml is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=2)
+            rows = list(self.rows)
+            if not rows:
+                return None
+            sm = sorted(r[0] for r in rows)
+            reasons = sorted({name for r in rows for bit, name in self.REASONS.items() if r[1] & bit})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(rows), "source": "nvml"}
+        if self.smi is None:
             return None
-        self.proc.terminate()
+        self.smi.terminate()
         try:
-            self.proc.wait(timeout=5)
+            self.smi.wait(timeout=5)
         except Exception:
-            self.proc.kill()
+            self.smi.kill()
         rows = []
         for line in open(self.path):
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
-                continue
-            if self.uuid and self.uuid not in parts[0]:
-                continue
-            rows.append(parts)
+            if len(parts) >= 7 and (not self.uuid or self.uuid in parts[0]):
+                rows.append(parts)
         os.unlink(self.path)
         if not rows:
             return None
         sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
         mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower().startswith("active")})
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi"}
 
 
 # --------------------------------------------------------------- CPU arm
@@ -206,8 +249,9 @@ def run_ours(args):
     do = torch.ones(B, H, L, E, device=dev, dtype=dt)
 
     def step(q, k, v, pair, do):
-        o, lse = nnop._flash_attention(q, k, v, pair, causal=causal)
-        return o, lse, nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=causal)
+        # the rrule's forward (keeping its workspace) and pullback
+        o, lse, ws = nnop._flash_attention_ws(q, k, v, pair, causal=causal)
+        return o, lse, nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=causal, fwd_workspace=ws)
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -222,7 +266,7 @@ def run_ours(args):
         uuid = str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
         pass
-    clocks = ClockSampler(uuid)
+    clocks = ClockSampler(uuid, local)
     clocks.start()
     barrier()
     torch.cuda.synchronize(dev)
@@ -231,9 +275,9 @@ def run_ours(args):
     t_start.record(stream)
     for i in range(K):
         ev[3 * i].record(stream)
-        o, lse = nnop._flash_attention(q, k, v, pair, causal=causal)
+        o, lse, ws = nnop._flash_attention_ws(q, k, v, pair, causal=causal)
         ev[3 * i + 1].record(stream)
-        nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=causal)
+        nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=causal, fwd_workspace=ws)
         ev[3 * i + 2].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
@@ -251,7 +295,7 @@ def run_ours(args):
     value = (fwd_f + bwd_f) * world / (ms / 1e3) / 1e12
 
     # ---- end to end through the public API with host buffers (pinned)
-    del o, lse
+    del o, lse, ws
     torch.cuda.empty_cache()
     host_in = [x.to("cpu").pin_memory() for x in (q, k, v, pair, do)]
     host_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in (q, k, v, pair)]
@@ -289,7 +333,7 @@ def run_ours(args):
     bwd_bytes = cfg_bytes(B, H, L, E, causal)[1]
     achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
     roofline = {
-        "kernel": "flash_attention_bwd call (fa_bwd_sm100_kernel + preprocess, pair_tiles_bwd, dq convert, dpair_from_tiles)",
+        "kernel": "flash_attention_bwd call (preprocess, fa_bwd_sm100_kernel, dq convert, dpair_from_tiles)",
         "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
         "peak_source": f"{src} hbm_gbs", "traffic": None,
         "algorithmic_bytes_per_launch": bwd_bytes, "launch_ms": bwd_ms,
@@ -313,8 +357,8 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (pair 4.29 GB per GPU)"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
-            # per step: pair_tiles_fwd, fa_fwd; preprocess, pair_tiles_bwd, fa_bwd, dq convert, dpair_from_tiles
-            "gpu_launches": K * 7,
+            # per step: pair_tiles, fa_fwd; preprocess, fa_bwd, dq convert, dpair_from_tiles
+            "gpu_launches": K * 6,
             "roofline": roofline,
             "clocks": clk,
         }

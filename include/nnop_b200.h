@@ -136,6 +136,37 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse,
                              int64_t QH, int64_t KH, int64_t B,
                              int causal, int dtype, void* stream);
 
+/*
+ * Backward reusing the forward's workspace: the forward (called with the same
+ * tensors, dimensions, causal flag and dtype, and a 256-byte aligned
+ * workspace of at least nnop_flash_attention_fwd_workspace_size(...) bytes)
+ * left the per-head pair tiles there, so the backward skips rebuilding them.
+ * This is the pullback of the reference's rrule (src/attention_crc.jl:16-31),
+ * which keeps the forward's state for `∇flash_attention`.  fwd_workspace may
+ * be NULL or hold no tiles (no pair bias, a shape or dtype the tensor-core
+ * kernels do not cover); the call is then nnop_flash_attention_bwd.  The pair
+ * must not change between the two calls.
+ *   workspace: >= nnop_flash_attention_bwd_workspace_size_reuse(...) bytes,
+ *   256-byte aligned.
+ */
+int nnop_flash_attention_bwd_reuse(const void* dO, const void* o, const float* lse,
+                                   const void* q, const void* k, const void* v,
+                                   const void* pair, const uint8_t* kpad_mask,
+                                   void* dq, void* dk, void* dv, void* dpair,
+                                   const void* fwd_workspace, size_t fwd_workspace_bytes,
+                                   void* workspace, size_t workspace_bytes,
+                                   int64_t E, int64_t QL, int64_t KL,
+                                   int64_t QH, int64_t KH, int64_t B,
+                                   int causal, int dtype, void* stream);
+
+/* Bytes of workspace nnop_flash_attention_bwd_reuse needs when the forward
+ * had fwd_workspace_bytes of workspace (less than
+ * nnop_flash_attention_bwd_workspace_size when the tiles are reused). */
+size_t nnop_flash_attention_bwd_workspace_size_reuse(int64_t E, int64_t QL, int64_t KL,
+                                                     int64_t QH, int64_t KH, int64_t B,
+                                                     int has_pair, size_t fwd_workspace_bytes,
+                                                     int dtype);
+
 /* --------------------------------------------------------------------------
  * Online softmax over the contiguous axis (Julia dims=1)
  * -------------------------------------------------------------------------- */

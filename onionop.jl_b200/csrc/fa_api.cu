@@ -26,10 +26,8 @@ int sm100_bwd_timeouts();
 namespace fa_host {
 size_t pair_tiles_bytes(int64_t QL, int64_t KL, int64_t H, int64_t B);
 template <typename T>
-int launch_pair_tiles_fwd(const T* pair, T* out, int64_t QL, int64_t KL, int H, int B, bool causal, cudaStream_t s);
-template <typename T>
-int launch_pair_tiles_bwd(const T* pair, T* out, const int* kv_len, int64_t QL, int64_t KL, int H, int B, bool causal,
-                          cudaStream_t s);
+int launch_pair_tiles(const T* pair, T* out, const int* kv_len, int64_t QL, int64_t KL, int H, int B, bool causal,
+                      cudaStream_t s);
 template <typename T>
 int launch_dpair_from_tiles(const T* tiles, T* dpair, const int* kv_len, int64_t QL, int64_t KL, int H, int B,
                             bool causal, cudaStream_t s);
@@ -76,13 +74,27 @@ struct BwdWorkspace {
     int* kv_len;
     float* delta;
     float* dq_acc;
-    void* pair_tiles;   // tcgen05 path with a pair bias: per-head pair tiles
-    void* ds_tiles;     // ... and the per-head dS tiles
+    void* ds_tiles;     // tcgen05 path with a pair bias: the per-head dS tiles
+    void* pair_tiles;   // ... and the per-head pair tiles (unless the forward's are reused)
     size_t bytes;
 };
 
+// Size the forward's workspace needs for the pair tiles (0: no tiles).
+size_t fwd_tiles_bytes(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t B, bool has_pair, int dtype) {
+    if (!has_pair || !pair_tiles_path(E, QH, dtype)) return 0;
+    return align256(fa_host::pair_tiles_bytes(QL, KL, QH, B));
+}
+
+// True when nnop_flash_attention_fwd, called with this workspace, wrote the
+// per-head pair tiles into it (the tcgen05 forward ran with a pair bias).
+bool fwd_keeps_tiles(const fa::Params& p, int dtype, const void* ws, size_t ws_bytes) {
+    const size_t need = fwd_tiles_bytes(p.E, p.QL, p.KL, p.QH, p.B, p.pair != nullptr, dtype);
+    const bool tiles = need > 0 && ws != nullptr && ws_bytes >= need && (reinterpret_cast<uintptr_t>(ws) & 255u) == 0;
+    return tiles && !force_mma() && fa::sm100_fwd_supported(p, dtype, true);
+}
+
 BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t B, bool has_pair,
-                        int dtype) {
+                        bool own_pair_tiles, int dtype) {
     BwdWorkspace w{};
     size_t off = 0;
     char* p = static_cast<char*>(base);
@@ -99,10 +111,12 @@ BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t KL, int64_t Q
     w.pair_tiles = w.ds_tiles = nullptr;
     if (has_pair && pair_tiles_path(E, QH, dtype)) {
         const size_t tb = align256(fa_host::pair_tiles_bytes(QL, KL, QH, B));
-        w.pair_tiles = p ? p + off : nullptr;
-        off += tb;
         w.ds_tiles = p ? p + off : nullptr;
         off += tb;
+        if (own_pair_tiles) {
+            w.pair_tiles = p ? p + off : nullptr;
+            off += tb;
+        }
     }
     w.bytes = off;
     return w;
@@ -110,9 +124,11 @@ BwdWorkspace bwd_layout(void* base, int64_t E, int64_t QL, int64_t KL, int64_t Q
 
 // f16/bf16 backward: delta, dq accumulator, the tcgen05 (or mma.sync) kernel,
 // dq conversion, and dpair (from the per-head dS tiles, or the zero fill of the
-// tiles the mma.sync kernel does not visit).
+// tiles the mma.sync kernel does not visit).  `fwd_tiles`: the forward's pair
+// tiles when they are reused, else nullptr (the tiles are built here).
 template <typename T>
-int bwd_16bit(fa::Params& p, const BwdWorkspace& ws, int64_t rows, bool causal, int dtype, cudaStream_t s) {
+int bwd_16bit(fa::Params& p, const BwdWorkspace& ws, const void* fwd_tiles, int64_t rows, bool causal, int dtype,
+              cudaStream_t s) {
     const int64_t E = p.E, QL = p.QL, KL = p.KL;
     const float sc = (float)(1.0 / sqrt((double)E));
     p.scale = std::is_same<T, __nv_bfloat16>::value ? __bfloat162float(__float2bfloat16_rn(sc))
@@ -120,16 +136,17 @@ int bwd_16bit(fa::Params& p, const BwdWorkspace& ws, int64_t rows, bool causal, 
     if (cudaMemsetAsync(ws.dq_acc, 0, (size_t)rows * E * sizeof(float), s) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: memset failed");
     p.dq_acc = ws.dq_acc;
-    const bool tc = !force_mma() && fa::sm100_bwd_supported(p, dtype) && (p.pair == nullptr || ws.pair_tiles);
+    const void* tiles = fwd_tiles ? fwd_tiles : ws.pair_tiles;
+    const bool tc = !force_mma() && fa::sm100_bwd_supported(p, dtype) && (p.pair == nullptr || (tiles && ws.ds_tiles));
     int st = fa_host::launch_preprocess<T>((const T*)p.dO, (const T*)p.o, ws.delta, rows, (int)E, s);
     if (st) return st;
     if (tc) {
-        if (p.pair) {
-            st = fa_host::launch_pair_tiles_bwd<T>((const T*)p.pair, (T*)ws.pair_tiles, p.kv_len, QL, KL, p.QH, p.B,
-                                                   causal, s);
+        if (p.pair && !fwd_tiles) {
+            st = fa_host::launch_pair_tiles<T>((const T*)p.pair, (T*)ws.pair_tiles, p.kv_len, QL, KL, p.QH, p.B,
+                                               causal, s);
             if (st) return st;
         }
-        st = fa::sm100_bwd(p, ws.pair_tiles, ws.ds_tiles, dtype, causal, s);
+        st = fa::sm100_bwd(p, tiles, ws.ds_tiles, dtype, causal, s);
     } else {
         st = fa::mma_bwd<T>(p, causal, s);
     }
@@ -159,8 +176,7 @@ size_t nnop_flash_attention_fwd_workspace_size(int64_t E, int64_t QL, int64_t KL
                                                int has_pair, int dtype) {
     (void)KH;
     if (E <= 0 || QL < 0 || KL < 0 || QH <= 0 || B < 0) return 0;
-    if (!has_pair || !pair_tiles_path(E, QH, dtype)) return 0;
-    return align256(fa_host::pair_tiles_bytes(QL, KL, QH, B));
+    return fwd_tiles_bytes(E, QL, KL, QH, B, has_pair != 0, dtype);
 }
 
 int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const void* pair,
@@ -195,11 +211,11 @@ int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const 
                                (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0;
             if (!force_mma() && fa::sm100_fwd_supported(p, dtype, tiles)) {
                 if (tiles) {
-                    st = bf ? fa_host::launch_pair_tiles_fwd<__nv_bfloat16>((const __nv_bfloat16*)pair,
-                                                                             (__nv_bfloat16*)workspace, QL, KL, (int)QH,
-                                                                             (int)B, causal != 0, s)
-                            : fa_host::launch_pair_tiles_fwd<__half>((const __half*)pair, (__half*)workspace, QL, KL,
-                                                                     (int)QH, (int)B, causal != 0, s);
+                    st = bf ? fa_host::launch_pair_tiles<__nv_bfloat16>((const __nv_bfloat16*)pair,
+                                                                         (__nv_bfloat16*)workspace, nullptr, QL, KL,
+                                                                         (int)QH, (int)B, causal != 0, s)
+                            : fa_host::launch_pair_tiles<__half>((const __half*)pair, (__half*)workspace, nullptr, QL,
+                                                                 KL, (int)QH, (int)B, causal != 0, s);
                     if (st) return st;
                 }
                 return fa::sm100_fwd(p, workspace, dtype, causal != 0, s);
@@ -214,13 +230,23 @@ size_t nnop_flash_attention_bwd_workspace_size(int64_t E, int64_t QL, int64_t KL
                                                int has_pair, int dtype) {
     (void)KH;
     if (E <= 0 || QL < 0 || KL < 0 || QH <= 0 || B < 0) return 0;
-    return bwd_layout(nullptr, E, QL, KL, QH, B, has_pair != 0, dtype).bytes;
+    return bwd_layout(nullptr, E, QL, KL, QH, B, has_pair != 0, true, dtype).bytes;
 }
 
-int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, const void* q, const void* k,
-                             const void* v, const void* pair, const uint8_t* kpad_mask, void* dq, void* dk,
-                             void* dv, void* dpair, void* workspace, size_t workspace_bytes, int64_t E, int64_t QL,
-                             int64_t KL, int64_t QH, int64_t KH, int64_t B, int causal, int dtype, void* stream) {
+size_t nnop_flash_attention_bwd_workspace_size_reuse(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH,
+                                                     int64_t B, int has_pair, size_t fwd_workspace_bytes, int dtype) {
+    (void)KH;
+    if (E <= 0 || QL < 0 || KL < 0 || QH <= 0 || B < 0) return 0;
+    const size_t need = fwd_tiles_bytes(E, QL, KL, QH, B, has_pair != 0, dtype);
+    const bool reuse = need > 0 && fwd_workspace_bytes >= need && (KL + 31) / 32 <= 2048;
+    return bwd_layout(nullptr, E, QL, KL, QH, B, has_pair != 0, !reuse, dtype).bytes;
+}
+
+int nnop_flash_attention_bwd_reuse(const void* dO, const void* o, const float* lse, const void* q, const void* k,
+                                   const void* v, const void* pair, const uint8_t* kpad_mask, void* dq, void* dk,
+                                   void* dv, void* dpair, const void* fwd_workspace, size_t fwd_workspace_bytes,
+                                   void* workspace, size_t workspace_bytes, int64_t E, int64_t QL, int64_t KL,
+                                   int64_t QH, int64_t KH, int64_t B, int causal, int dtype, void* stream) {
     int st = check_dims(E, QL, KL, QH, KH, B, dtype);
     if (st) return st;
     if ((pair == nullptr) != (dpair == nullptr))
@@ -241,21 +267,22 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, co
     if (!aligned16(dO) || !aligned16(o) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dq) ||
         !aligned16(dk) || !aligned16(dv))
         return fail(NNOP_ERR_ALIGN, "flash_attention_bwd: dense tensors must be 16-byte aligned");
-    BwdWorkspace ws = bwd_layout(workspace, E, QL, KL, QH, B, pair != nullptr, dtype);
+    fa::Params p{};
+    p.q = q; p.k = k; p.v = v; p.pair = pair; p.kmask = kpad_mask; p.o = const_cast<void*>(o);
+    p.lse = const_cast<float*>(lse); p.dO = dO;
+    p.dq = dq; p.dk = dk; p.dv = dv; p.dpair = dpair;
+    p.QL = QL; p.KL = KL; p.E = (int)E; p.QH = (int)QH; p.KH = (int)KH; p.B = (int)B;
+    p.n_rep = (int)(QH / KH);
+    const bool reuse = pair != nullptr && dtype != NNOP_F32 && fwd_keeps_tiles(p, dtype, fwd_workspace, fwd_workspace_bytes);
+    BwdWorkspace ws = bwd_layout(workspace, E, QL, KL, QH, B, pair != nullptr, !reuse, dtype);
     if (!workspace || workspace_bytes < ws.bytes)
         return fail(NNOP_ERR_WORKSPACE, "flash_attention_bwd: workspace too small (need " + std::to_string(ws.bytes) +
                                             " bytes)");
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
         return fail(NNOP_ERR_ALIGN, "flash_attention_bwd: workspace must be 256-byte aligned");
     cudaStream_t s = (cudaStream_t)stream;
-
-    fa::Params p{};
-    p.q = q; p.k = k; p.v = v; p.pair = pair; p.kmask = kpad_mask; p.o = const_cast<void*>(o);
-    p.lse = const_cast<float*>(lse); p.dO = dO; p.delta = ws.delta;
+    p.delta = ws.delta;
     p.kv_len = kpad_mask ? ws.kv_len : nullptr;
-    p.dq = dq; p.dk = dk; p.dv = dv; p.dpair = dpair;
-    p.QL = QL; p.KL = KL; p.E = (int)E; p.QH = (int)QH; p.KH = (int)KH; p.B = (int)B;
-    p.n_rep = (int)(QH / KH);
     const int64_t rows = B * QH * QL;
 
     if (kpad_mask) {
@@ -278,11 +305,19 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, co
             return st;
         }
         case NNOP_F16:
-            return bwd_16bit<__half>(p, ws, rows, c, dtype, s);
+            return bwd_16bit<__half>(p, ws, reuse ? fwd_workspace : nullptr, rows, c, dtype, s);
         case NNOP_BF16:
-            return bwd_16bit<__nv_bfloat16>(p, ws, rows, c, dtype, s);
+            return bwd_16bit<__nv_bfloat16>(p, ws, reuse ? fwd_workspace : nullptr, rows, c, dtype, s);
     }
     return fail(NNOP_ERR_DTYPE, "flash_attention_bwd: unsupported dtype");
+}
+
+int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, const void* q, const void* k,
+                             const void* v, const void* pair, const uint8_t* kpad_mask, void* dq, void* dk,
+                             void* dv, void* dpair, void* workspace, size_t workspace_bytes, int64_t E, int64_t QL,
+                             int64_t KL, int64_t QH, int64_t KH, int64_t B, int causal, int dtype, void* stream) {
+    return nnop_flash_attention_bwd_reuse(dO, o, lse, q, k, v, pair, kpad_mask, dq, dk, dv, dpair, nullptr, 0,
+                                          workspace, workspace_bytes, E, QL, KL, QH, KH, B, causal, dtype, stream);
 }
 
 }  // extern "C"

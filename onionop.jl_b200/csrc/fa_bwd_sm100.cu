@@ -7,23 +7,26 @@
 // for GQA.  Here one CTA owns a 128-key tile of one KV head of one batch and
 // walks the 128-query tiles of every query head of its GQA group; dK and dV
 // stay in TMEM for the whole walk.  Per step (query tile i):
-//   Sᵀ  = K·Q_iᵀ           (keys on TMEM lanes)       UMMA ss
+//   Sᵀ  = K·Q_iᵀ (+ c·I·pairᵀ)  (keys on TMEM lanes)   UMMA ss
 //   dPᵀ = V·dO_iᵀ                                       UMMA ss
-//   Pᵀ  = exp(Sᵀ·scale + pairᵀ − lse_i),  dSᵀ = Pᵀ∘(dPᵀ − δ_i)   (elementwise)
+//   Pᵀ  = exp(Sᵀ·scale − lse_i),  dSᵀ = Pᵀ∘(dPᵀ − δ_i)   (elementwise)
 //   dV += Pᵀ·dO_i   (Pᵀ from TMEM)                      UMMA ts
 //   dK += dSᵀ·Q_i   (dSᵀ from TMEM)                     UMMA ts
 //   dQ_i = dS·K     (dS from shared memory, MN-major)   UMMA ss
 //   dq_acc[i] += scale·dQ_i  (fp32 vector reductions, red.global.add.v4.f32)
 //   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
-//                 written per head as dS tiles, see pair_tiles.cu.
+//                 written per head as key-major dS tiles, see pair_tiles.cu.
+// The pair bias enters through the tensor cores: c = 1/scale (a power of two,
+// so c·pair is exact in the fp32 accumulator) times the shifted identity of
+// fa_sm100.cuh as A, the pair tile [key][query] of the key-major per-head copy
+// pair_tiles() writes as the MN-major B operand.
 // Warp roles (512 threads):
 //   warp 0      TMA producer (K, V once; Q_i, dO_i into a 2-stage ring)
 //   warp 1      MMA issuer (one lane)
 //   warps 2-3   tile provider: lse_i (log2 units) and δ_i
-//   (the pair tile of (query tile, key tile, head) is a TMA box of the per-head
-//   copy pair_tiles_bwd() writes, [B][H][QL/8][KL][8], issued by warp 0; dS
-//   goes out as 16-byte rows in the same layout and dpair_from_tiles() turns
-//   it into dpair)
+//   (the pair tile of (query tile, key tile, head), two 64-query boxes of
+//   [B][H][KL][QL], is also loaded by warp 0; dS goes out as 32-byte row
+//   pieces in the same layout and dpair_from_tiles() turns it into dpair)
 //   warps 4-11  elementwise: two warpgroups on the same 128 TMEM lanes
 //               (one key per lane), query columns [0,64) and [64,128)
 //   warps 12-15 dQ: TMEM dQ rows -> fp32 reductions into the accumulator
@@ -63,7 +66,7 @@ enum Bar {
     kTileEmpty = 11,  // +buffer: elementwise -> provider (256 arrivals)
     kFinal = 13,      // every MMA retired
     kPairFull = 14,   // +buffer: pair tile landed (TMA)
-    kPairEmpty = 16,  // +buffer: elementwise done with it (256 arrivals)
+    kPairEmpty = 16,  // +buffer: its UMMAs retired
     kNumBars = 18
 };
 
@@ -74,9 +77,10 @@ struct Lay {
     static constexpr int kQ = kV + kTile;           // 2 stages
     static constexpr int kDO = kQ + 2 * kTile;      // 2 stages
     static constexpr int kDS = kDO + 2 * kTile;     // [2 halves][128 keys][64 queries], MN-major SW128
-    static constexpr int kPair = kDS + 2 * kTile;   // 2 buffers of [BM/8][BN][8]
+    static constexpr int kPair = kDS + 2 * kTile;   // 2 buffers of [2 halves][BN keys][64 queries] SW128
     static constexpr int kPairBytes = kBM * kBN * 2;
-    static constexpr int kLse = kPair + 2 * kPairBytes;   // [2][BM] float (log2 units)
+    static constexpr int kEye = kPair + 2 * kPairBytes;   // shifted identity (1024-aligned)
+    static constexpr int kLse = kEye + kEyeBytes;         // [2][BM] float (log2 units)
     static constexpr int kDel = kLse + 2 * kBM * 4;       // [2][BM] float
     static constexpr int kBar = kDel + 2 * kBM * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
@@ -87,9 +91,6 @@ struct Lay {
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
     asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                  : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 // Warp-uniform bounded wait: true only if every lane saw the phase complete
 // (guards warp-wide tcgen05.ld/st, which must not run divergent).
@@ -134,7 +135,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             mbar_init(&bars[kTileFull + s], 64);
             mbar_init(&bars[kTileEmpty + s], 256);
             mbar_init(&bars[kPairFull + s], 1);
-            mbar_init(&bars[kPairEmpty + s], 256);
+            mbar_init(&bars[kPairEmpty + s], 1);
         }
         mbar_init(&bars[kSFull], 1);
         mbar_init(&bars[kPFull], 256);
@@ -142,6 +143,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_init(&bars[kDQEmpty], 128);
         mbar_init(&bars[kFinal], 1);
         fence_mbar_init();
+    }
+    if (PAIR) {
+        build_eye<T>(smem + Lay::kEye, 1.f / p.scale, threadIdx.x, kThreads);
+        fence_proxy_async_smem();   // identity writes -> UMMA reads
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -178,8 +183,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tma_load_3d(smem + Lay::kDO + s * Lay::kTile, &tm_do, &bars[kQFull + s], 0, q0, b * QH + h);
                 if (PAIR) {
                     mbar_expect_tx(&bars[kPairFull + s], Lay::kPairBytes);
-                    tma_load_3d(smem + Lay::kPair + s * Lay::kPairBytes, &tm_pair, &bars[kPairFull + s], 0, (int)k0,
-                                (int)(((int64_t)b * QH + h) * (qlp / 8) + q0 / 8));
+#pragma unroll
+                    for (int half = 0; half < 2; ++half)
+                        tma_load_3d(smem + Lay::kPair + s * Lay::kPairBytes + half * kBN * 128, &tm_pair,
+                                    &bars[kPairFull + s], q0 + half * 64, (int)k0, b * QH + h);
                 }
             }
             // copies in flight land before the CTA leaves (bounded waits)
@@ -195,11 +202,14 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t id_kv = idesc_f16<kBF16>(128, 64, false, true);    // dV, dK (A in TMEM)
         constexpr uint32_t id_q = idesc_f16<kBF16>(128, 64, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
+        constexpr uint32_t id_p = idesc_f16<kBF16>(128, 128, false, true);   // Sᵀ += c·I·pairᵀ
         const uint32_t sDS = smem_u32(smem + Lay::kDS);
+        const uint32_t sEye = smem_u32(smem + Lay::kEye);
         bool ok = steps > 0 && wait_warp(&bars[kKVFull], 0, ab, 4);
         for (int st = 0; ok && st < steps; ++st) {
             const int s = st & 1;
             if (!wait_warp(&bars[kQFull + s], (st >> 1) & 1, ab, 5)) break;
+            if (PAIR && !wait_warp(&bars[kPairFull + s], (st >> 1) & 1, ab, 16)) break;
             tc_fence_after();
             const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile);
             const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile);
@@ -208,6 +218,15 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 for (int kk = 0; kk < kE / 16; ++kk) {
                     umma_ss(tS, desc_k_sw128(sK + kk * 32), desc_k_sw128(sQ + kk * 32), id_s, kk > 0 ? 1u : 0u);
                     umma_ss(tDP, desc_k_sw128(sV + kk * 32), desc_k_sw128(sDO + kk * 32), id_s, kk > 0 ? 1u : 0u);
+                }
+                if (PAIR) {
+                    // B = pair tile [key][query]: MN-major over queries, K = keys
+                    const uint32_t sP = smem_u32(smem + Lay::kPair + s * Lay::kPairBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBN / 16; ++kk)
+                        umma_ss(tS, desc_k_sw128(eye_step(sEye, kk)), desc_mn_sw128(sP + kk * 16 * 128, kBN * 128),
+                                id_p, 1u);
+                    umma_commit(&bars[kPairEmpty + s]);
                 }
                 umma_commit(&bars[kSFull]);
             }
@@ -272,11 +291,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const int h = kvh * p.n_rep + st / nq;
             const int64_t q0 = (int64_t)(qt0 + st % nq) * kBM;
             if (!wait_warp(&bars[kTileFull + buf], (st >> 1) & 1, ab, 10)) break;
-            if (PAIR && !wait_warp(&bars[kPairFull + buf], (st >> 1) & 1, ab, 16)) break;
             if (!wait_warp(&bars[kSFull], st & 1, ab, 11)) break;
             tc_fence_after();
-            // dS tile rows of this key: [b][h][query/8][key][8]
-            uint16_t* dst_row = PAIR ? ds_tiles + ((((int64_t)b * QH + h) * (qlp / 8) + q0 / 8) * klp + j) * 8 : nullptr;
+            // dS tile row of this key: [b][h][key][query]
+            uint16_t* dst_row = PAIR ? ds_tiles + (((int64_t)b * QH + h) * klp + j) * qlp + q0 : nullptr;
 #pragma unroll 1
             for (int cc = 0; cc < 4; ++cc) {
                 const int col = c0 + cc * 16;
@@ -284,18 +302,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tmem_ld16(tS + lane_off + col, sr);
                 tmem_ld16(tDP + lane_off + col, dr);
                 tmem_ld_wait();
-                float pb[16];
-                if (PAIR) {
-                    const uint8_t* src = smem + Lay::kPair + buf * Lay::kPairBytes;
-#pragma unroll
-                    for (int g = 0; g < 2; ++g) {
-                        const uint4 u = *reinterpret_cast<const uint4*>(src + ((((col >> 3) + g) * kBN + jr) * 8) * 2);
-                        float f8[8];
-                        unpack8<T>(u, f8);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) pb[g * 8 + e] = f8[e] * kLog2e;
-                    }
-                }
                 uint32_t pk[8], dk[8];
 #pragma unroll
                 for (int t = 0; t < 16; t += 2) {
@@ -306,8 +312,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                         const int64_t i = q0 + c;
                         bool valid = key_ok && i < QL;
                         if (CAUSAL) valid = valid && (j <= i);
-                        float x = __uint_as_float(sr[t + u]) * sl2 - sLse[buf * kBM + c];
-                        if (PAIR) x += pb[t + u];
+                        const float x = __uint_as_float(sr[t + u]) * sl2 - sLse[buf * kBM + c];
                         const float pr = valid ? ex2(x) : 0.f;
                         pv[u] = pr;
                         dv[u] = pr * (__uint_as_float(dr[t + u]) - sDel[buf * kBM + c]);
@@ -330,12 +335,11 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 if (PAIR) {
 #pragma unroll
                     for (int v = 0; v < 2; ++v)
-                        __stcs(reinterpret_cast<uint4*>(dst_row + (int64_t)((col >> 3) + v) * klp * 8),
+                        __stcs(reinterpret_cast<uint4*>(dst_row + col + v * 8),
                                make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]));
                 }
             }
             mbar_arrive(&bars[kTileEmpty + buf]);
-            if (PAIR) mbar_arrive(&bars[kPairEmpty + buf]);
             tmem_st_wait();
             fence_proxy_async_smem();   // dS smem writes -> tensor-core (async proxy) reads
             tc_fence_before();
@@ -400,21 +404,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
 }
 
-// 3-D map over the per-head backward pair tiles [B·H·QLp/8][KLp][8], box
-// (8, 128, 16): one (128-key, 128-query) tile as [query/8][key][8].
-bool make_pair_tiles_map_bwd(CUtensorMap* m, const void* base, int64_t klp, int64_t rows, bool bf16) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[3] = {8, (cuuint64_t)klp, (cuuint64_t)rows};
-    cuuint64_t strides[2] = {16, (cuuint64_t)klp * 16};
-    cuuint32_t box[3] = {8, (cuuint32_t)kBN, (cuuint32_t)(kBM / 8)};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 template <typename T, bool CAUSAL, bool PAIR, bool MASK>
 int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t s) {
     constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -425,7 +414,7 @@ int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t
         !make_map(&tk, p.k, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
-        (PAIR && !make_pair_tiles_map_bwd(&tp, pair_tiles, klp, (int64_t)p.B * p.QH * (qlp / 8), bf16)))
+        (PAIR && !make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16)))
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_bwd_sm100_kernel<T, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)

@@ -7,12 +7,16 @@
 // One CTA per (128-query tile, query head, batch); 256 threads:
 //   warp 0     TMA producer: Q once, then K_j / V_j into a 2-stage ring and,
 //              with a pair bias, the pair tile of (q-tile, k-tile j, head)
-//              from the per-head copy pair_tiles_fwd() writes (layout
-//              [B][H][KL/8][QL][8], so the box lands as [key/8][query][8]);
+//              from the key-major per-head copy pair_tiles() writes
+//              ([B][H][KL][QL], two 64-query boxes: [key][query] per half);
 //   warp 1     MMA issuer: S_j = Q·K_jᵀ into one of two TMEM score buffers,
+//              plus, with a pair bias, S_j += c·I·pair_jᵀ (c = 1/scale; the
+//              pair tile is the K-major B operand of a 128x128x128 UMMA
+//              whose A is the shifted identity of fa_sm100.cuh -- exact,
+//              since c is a power of two and products accumulate in fp32),
 //              O += P_j·V_j with P_j read from TMEM (tcgen05 "ts" form);
 //   warps 4-7  softmax: thread r owns query row r (TMEM lane r): it reads
-//              its 128 scores, adds the pair bias, masks, updates the running
+//              its 128 scores (bias included), masks, updates the running
 //              max (rescaling O in TMEM only when the max grows by more than
 //              2^8 -- the stale max keeps exp2 values <= 256), writes P as
 //              16-bit values back into the score columns, and finally
@@ -53,8 +57,8 @@ enum Bar {
     kPFull = 9,      // +buffer
     kOFinal = 11,
     kOStep = 12,
-    kPairFull = 13,  // +buffer (TMA -> softmax)
-    kPairEmpty = 15, // +buffer (softmax -> producer)
+    kPairFull = 13,  // +buffer (TMA -> MMA)
+    kPairEmpty = 15, // +buffer (its UMMAs retired -> producer)
     kMmaDone = 17,   // MMA warp's own "all my MMAs retired" barrier
     kNumBars = 18
 };
@@ -68,7 +72,8 @@ struct Layout {
     static constexpr int kV = kK + kStages * kKVBytes;
     static constexpr int kPairBytes = PAIR ? kBN * kBM * 2 : 0;
     static constexpr int kPair = kV + kStages * kKVBytes;
-    static constexpr int kBits = kPair + 2 * kPairBytes;        // kMaxKeyWords uint32
+    static constexpr int kEye = kPair + 2 * kPairBytes;         // shifted identity (1024-aligned)
+    static constexpr int kBits = kEye + (PAIR ? kEyeBytes : 0); // kMaxKeyWords uint32
     static constexpr int kBar = kBits + kMaxKeyWords * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kTotal = kTmemSlot + 16;
@@ -85,7 +90,7 @@ template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_pair,
-                    const Params p, int64_t kl_pad) {
+                    const Params p) {
     using L = Layout<E, PAIR>;
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
@@ -129,6 +134,10 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             bits[w] = n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
         }
     }
+    if (PAIR) {
+        build_eye<T>(smem + L::kEye, 1.f / p.scale, threadIdx.x, kThreads);
+        fence_proxy_async_smem();   // identity writes -> UMMA reads
+    }
     if (threadIdx.x == 0) {
         s_abort = 0;
         mbar_init(&bars[kQFull], 1);
@@ -141,7 +150,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             mbar_init(&bars[kSFull + i], 1);
             mbar_init(&bars[kPFull + i], 128);
             mbar_init(&bars[kPairFull + i], 1);
-            mbar_init(&bars[kPairEmpty + i], 128);
+            mbar_init(&bars[kPairEmpty + i], 1);
         }
         mbar_init(&bars[kOFinal], 1);
         mbar_init(&bars[kOStep], 1);
@@ -173,7 +182,6 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             tma_prefetch(&tm_v);
             if (PAIR) tma_prefetch(&tm_pair);
             const int bh_q = b * p.QH + h, bh_k = b * p.KH + kvh;
-            const int64_t pair_row0 = ((int64_t)b * p.QH + h) * (kl_pad / 8);
             mbar_expect_tx(&bars[kQFull], L::kQBytes);
 #pragma unroll
             for (int half = 0; half < E / 64; ++half)
@@ -197,8 +205,10 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                                 half * 64, k0, bh_k);
                 if (PAIR) {
                     mbar_expect_tx(&bars[kPairFull + (j & 1)], L::kPairBytes);
-                    tma_load_3d(smem + L::kPair + (j & 1) * L::kPairBytes, &tm_pair, &bars[kPairFull + (j & 1)], 0,
-                                (int)q0, (int)(pair_row0 + k0 / 8));
+#pragma unroll
+                    for (int half = 0; half < 2; ++half)
+                        tma_load_3d(smem + L::kPair + (j & 1) * L::kPairBytes + half * kBN * 128, &tm_pair,
+                                    &bars[kPairFull + (j & 1)], (int)q0 + half * 64, k0, bh_q);
                 }
             }
             // Copies still in flight must land before the CTA can exit (they
@@ -216,9 +226,11 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t idesc_o = idesc_f16<kBF16>(kBM, E, false, true);
         const uint32_t sQ = smem_u32(smem + L::kQ);
         bool ok = n_kt > 0 && wait_warp(&bars[kQFull], 0, ab, 7);
+        const uint32_t sEye = smem_u32(smem + L::kEye);
         auto issue_s = [&](int j) -> bool {
             const int s = j % kStages;
             if (!wait_warp(&bars[kKFull + s], (j / kStages) & 1, ab, 8)) return false;
+            if (PAIR && !wait_warp(&bars[kPairFull + (j & 1)], (j >> 1) & 1, ab, 12)) return false;
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t sK = smem_u32(smem + L::kK + s * L::kKVBytes);
@@ -228,6 +240,15 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     const uint32_t off_q = (kk / 4) * kBM * 128 + (kk % 4) * 32;
                     const uint32_t off_k = (kk / 4) * kBN * 128 + (kk % 4) * 32;
                     umma_ss(d, desc_k_sw128(sQ + off_q), desc_k_sw128(sK + off_k), idesc_s, kk > 0 ? 1u : 0u);
+                }
+                if (PAIR) {
+                    // S += c·I·pairᵀ: B = pair tile [key][query], K-major over queries
+                    const uint32_t sP = smem_u32(smem + L::kPair + (j & 1) * L::kPairBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBM / 16; ++kk)
+                        umma_ss(d, desc_k_sw128(eye_step(sEye, kk)),
+                                desc_k_sw128(sP + (kk / 4) * kBN * 128 + (kk % 4) * 32), idesc_s, 1u);
+                    umma_commit(&bars[kPairEmpty + (j & 1)]);
                 }
                 umma_commit(&bars[kSFull + (j & 1)]);
             }
@@ -272,7 +293,6 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int j = 0; j < n_kt; ++j) {
             const int buf = j & 1;
             const int64_t k0 = (int64_t)j * kBN;
-            if (PAIR && !wait_warp(&bars[kPairFull + buf], (j >> 1) & 1, ab, 12)) { ok = false; break; }
             if (!wait_warp(&bars[kSFull + buf], (j >> 1) & 1, ab, 13)) { ok = false; break; }
             tc_fence_after();
             const uint32_t tS = (buf ? tS1 : tS0) + lane_off;
@@ -284,28 +304,14 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tmem_ld_wait();
                 // words past the last key are never read: k0 + c·32 < n_words·32 here
                 const uint32_t vbits = (k0 + c * 32 < KL) ? bits[(k0 >> 5) + c] : 0u;
-                float pb[32];
-                if (PAIR) {
-                    const uint8_t* src = smem + L::kPair + buf * L::kPairBytes;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const uint4 u = *reinterpret_cast<const uint4*>(src + (((c * 4 + g) * kBM + r) * 8) * 2);
-                        float f8[8];
-                        unpack8<T>(u, f8);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) pb[g * 8 + e] = f8[e] * kLog2e;
-                    }
-                }
 #pragma unroll
                 for (int t = 0; t < 32; ++t) {
-                    float v = __uint_as_float(raw[t]) * sl2;
-                    if (PAIR) v += pb[t];
+                    const float v = __uint_as_float(raw[t]) * sl2;
                     bool valid = (vbits >> t) & 1u;
                     if (CAUSAL) valid = valid && (k0 + c * 32 + t <= i);
                     x[c * 32 + t] = valid ? v : -INFINITY;
                 }
             }
-            if (PAIR) mbar_arrive(&bars[kPairEmpty + buf]);
             float mx = x[0];
 #pragma unroll
             for (int t = 1; t < kBN; ++t) mx = fmaxf(mx, x[t]);
@@ -392,21 +398,6 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
 }
 
-// 3-D map over the per-head pair tiles [B·H·KLp/8][QLp][8] (see
-// pair_tiles_fwd), box (8, 128, 16): one (128-query, 128-key) tile.
-bool make_pair_tiles_map(CUtensorMap* m, const void* base, int64_t qlp, int64_t rows, bool bf16) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[3] = {8, (cuuint64_t)qlp, (cuuint64_t)rows};
-    cuuint64_t strides[2] = {16, (cuuint64_t)qlp * 16};
-    cuuint32_t box[3] = {8, (cuuint32_t)kBM, (cuuint32_t)(kBN / 8)};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
 int launch(const Params& p, const void* pair_tiles, cudaStream_t s) {
     using Lay = Layout<E, PAIR>;
@@ -417,13 +408,13 @@ int launch(const Params& p, const void* pair_tiles, cudaStream_t s) {
     if (!make_map(&tq, p.q, E, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
-        (PAIR && !make_pair_tiles_map(&tp, pair_tiles, qlp, (int64_t)p.B * p.QH * (klp / 8), bf16)))
+        (PAIR && !make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16)))
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_fwd_sm100_kernel<T, E, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cannot set shared memory size");
     dim3 grid(p.QH, (unsigned)((p.QL + kBM - 1) / kBM), p.B);
-    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tp, p, klp);
+    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tp, p);
     return check_launch("flash_attention_fwd (sm100)");
 }
 

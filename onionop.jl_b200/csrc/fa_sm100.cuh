@@ -38,6 +38,31 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
     for (int i = 0; i < 8; ++i) f[i] = to_f(h[i]);
 }
 
+// Shifted identity for the pair-bias UMMA (scores += c·I · pair tile): 192
+// rows of a K-major 128-byte-swizzled operand (1024-byte aligned) holding c at
+// (row 64+m, column m) for m < 64 and zeros elsewhere.  K16 step kk of a
+// 128x128x128 product reads rows [64, 192) (kk < 4) or [0, 128) (kk >= 4) at
+// column block kk%4: that is c times the 128x128 identity restricted to
+// columns [16kk, 16kk+16).
+constexpr int kEyeBytes = 192 * 128;
+
+template <typename T>
+__device__ __forceinline__ void build_eye(uint8_t* eye, float c, int tid, int nthreads) {
+    const uint32_t cb = pack16<T>(c, 0.f) & 0xffffu;
+    for (int u = tid; u < kEyeBytes / 16; u += nthreads) {
+        const int row = u >> 3, chunk = (u & 7) ^ (row & 7);   // logical 8-column chunk
+        const int m = row - 64;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (m >= 0 && m < 64 && (m >> 3) == chunk) w[(m & 7) >> 1] = cb << (16 * (m & 1));
+        reinterpret_cast<uint4*>(eye)[u] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// Start address of K16 step kk of the shifted identity.
+__device__ __forceinline__ uint32_t eye_step(uint32_t eye, int kk) {
+    return eye + (kk < 4 ? 64 * 128 : 0) + (kk & 3) * 32;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

@@ -113,6 +113,14 @@ def _fa_dims(q, k, v, pair, kpad_mask):
 def _flash_attention(q, k, v, pair=None, *, causal: bool, kpad_mask=None):
     """Forward returning ``(o, lse)`` (``_flash_attention``, src/attention.jl:177-229,
     which returns ``(o, ms, ls)``; here ``lse = ms + log(ls)`` in float32)."""
+    o, lse, _ = _flash_attention_ws(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)
+    return o, lse
+
+
+def _flash_attention_ws(q, k, v, pair=None, *, causal: bool, kpad_mask=None):
+    """``_flash_attention`` that also returns its workspace (None or a uint8
+    tensor holding the per-head pair tiles) for ``grad_flash_attention``'s
+    ``fwd_workspace``: the rrule's forward state."""
     dev = _dev(q, k, v, pair, kpad_mask)
     B, QH, QL, E, KH, KL = _fa_dims(q, k, v, pair, kpad_mask)
     q, k, v, pair = _contig(q), _contig(k), _contig(v), _contig(pair)
@@ -125,12 +133,14 @@ def _flash_attention(q, k, v, pair=None, *, causal: bool, kpad_mask=None):
     check(lib.nnop_flash_attention_fwd(
         _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m), _ptr(o), _ptr(lse), _ptr(ws), ws_bytes,
         E, QL, KL, QH, KH, B, int(bool(causal)), dt, _stream(dev)))
-    return o, lse
+    return o, lse, ws
 
 
-def grad_flash_attention(do, o, lse, q, k, v, pair=None, *, causal: bool, kpad_mask=None):
+def grad_flash_attention(do, o, lse, q, k, v, pair=None, *, causal: bool, kpad_mask=None, fwd_workspace=None):
     """``∇flash_attention`` (src/attention_bwd.jl:213-303): returns
-    ``(dq, dk, dv, dpair)``, dpair None when pair is None."""
+    ``(dq, dk, dv, dpair)``, dpair None when pair is None.  ``fwd_workspace``:
+    the workspace ``_flash_attention_ws`` returned for the same inputs; its
+    pair tiles are then reused instead of rebuilt."""
     dev = _dev(do, o, lse, q, k, v, pair, kpad_mask)
     B, QH, QL, E, KH, KL = _fa_dims(q, k, v, pair, kpad_mask)
     do, o, q, k, v, pair = map(_contig, (do, o, q, k, v, pair))
@@ -141,11 +151,13 @@ def grad_flash_attention(do, o, lse, q, k, v, pair=None, *, causal: bool, kpad_m
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dpair = torch.empty_like(pair) if pair is not None else None
     dt = _dtype_id(q)
-    ws_bytes = lib.nnop_flash_attention_bwd_workspace_size(E, QL, KL, QH, KH, B, int(pair is not None), dt)
+    fw_bytes = 0 if fwd_workspace is None else fwd_workspace.numel()
+    ws_bytes = lib.nnop_flash_attention_bwd_workspace_size_reuse(E, QL, KL, QH, KH, B, int(pair is not None),
+                                                                  fw_bytes, dt)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-    check(lib.nnop_flash_attention_bwd(
+    check(lib.nnop_flash_attention_bwd_reuse(
         _ptr(do), _ptr(o), _ptr(lse), _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m),
-        _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dpair), _ptr(ws), ws_bytes,
+        _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dpair), _ptr(fwd_workspace), fw_bytes, _ptr(ws), ws_bytes,
         E, QL, KL, QH, KH, B, int(bool(causal)), dt, _stream(dev)))
     return dq, dk, dv, dpair
 
@@ -155,16 +167,16 @@ class _FlashAttentionFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, pair, kpad_mask, causal):
-        o, lse = _flash_attention(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)
-        ctx.save_for_backward(o, lse, q, k, v, pair, kpad_mask)
+        o, lse, ws = _flash_attention_ws(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)
+        ctx.save_for_backward(o, lse, q, k, v, pair, kpad_mask, ws)
         ctx.causal = causal
         return o
 
     @staticmethod
     def backward(ctx, do):
-        o, lse, q, k, v, pair, kpad_mask = ctx.saved_tensors
+        o, lse, q, k, v, pair, kpad_mask, ws = ctx.saved_tensors
         dq, dk, dv, dpair = grad_flash_attention(do, o, lse, q, k, v, pair, causal=ctx.causal,
-                                                 kpad_mask=kpad_mask)
+                                                 kpad_mask=kpad_mask, fwd_workspace=ws)
         return dq, dk, dv, dpair, None, None
 
 

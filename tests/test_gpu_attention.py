@@ -21,7 +21,7 @@ ABS_FLOOR = {"f32": 1e-6, "f16": 1e-3, "bf16": 1e-3}
 
 
 def run_case(B, QH, KH, QL, KL, E, dtype, causal, use_pair, use_mask, seed=0, dO_ones=False,
-             mask_fn=None, pair_scale=1.0):
+             mask_fn=None, pair_scale=1.0, reuse=False, pair_fn=None):
     import nnop
     rng = np.random.default_rng(seed)
     q = rng.standard_normal((B, QH, QL, E)).astype(np.float32)
@@ -29,6 +29,8 @@ def run_case(B, QH, KH, QL, KL, E, dtype, causal, use_pair, use_mask, seed=0, dO
     v = rng.standard_normal((B, KH, KL, E)).astype(np.float32)
     do = np.ones((B, QH, QL, E), np.float32) if dO_ones else rng.standard_normal((B, QH, QL, E)).astype(np.float32)
     pair = (pair_scale * rng.standard_normal((B, KL, QL, QH))).astype(np.float32) if use_pair else None
+    if pair_fn is not None:
+        pair_fn(pair, rng)
     mask = None
     if use_mask:
         mask = np.ones((B, KL), bool)
@@ -42,8 +44,13 @@ def run_case(B, QH, KH, QL, KL, E, dtype, causal, use_pair, use_mask, seed=0, dO
     pd = to_dev(pair, dtype) if use_pair else None
     import torch
     md = torch.from_numpy(mask).cuda() if use_mask else None
-    o, lse = nnop._flash_attention(qd, kd, vd, pd, causal=causal, kpad_mask=md)
-    dq, dk, dv, dpair = nnop.grad_flash_attention(dod, o, lse, qd, kd, vd, pd, causal=causal, kpad_mask=md)
+    if reuse:
+        o, lse, ws = nnop._flash_attention_ws(qd, kd, vd, pd, causal=causal, kpad_mask=md)
+        dq, dk, dv, dpair = nnop.grad_flash_attention(dod, o, lse, qd, kd, vd, pd, causal=causal, kpad_mask=md,
+                                                      fwd_workspace=ws)
+    else:
+        o, lse = nnop._flash_attention(qd, kd, vd, pd, causal=causal, kpad_mask=md)
+        dq, dk, dv, dpair = nnop.grad_flash_attention(dod, o, lse, qd, kd, vd, pd, causal=causal, kpad_mask=md)
     torch.cuda.synchronize()
     scale = orc.attention_scale(E, dtype)
     args = dict(causal=causal, kpad_mask=mask, scale=scale)
@@ -202,3 +209,58 @@ def test_attention_errors():
         nnop.flash_attention(q, k, k, causal=False)
     with pytest.raises(nnop.NNopShapeError, match="Shapes of K"):
         nnop.flash_attention(q, k, torch.zeros(1, 2, 9, 64, device="cuda", dtype=torch.bfloat16), causal=False)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_attention_bwd_reuses_forward_tiles(dtype):
+    """nnop_flash_attention_bwd_reuse: the backward reads the pair tiles the
+    forward left in its workspace; results equal the rebuilding backward's
+    bit for bit (dq aside: its fp32 reductions land in any order) and match
+    the oracle (causal, padding mask, GQA, ragged)."""
+    for (B, QH, KH, QL, KL, causal, use_mask) in [(2, 4, 2, 300, 421, False, True), (2, 4, 4, 257, 257, True, True),
+                                                  (1, 8, 2, 513, 300, True, False), (1, 2, 2, 128, 128, False, False)]:
+        kw = dict(seed=QL + KL, use_pair=True, use_mask=use_mask)
+        got_r, want = run_case(B, QH, KH, QL, KL, 64, dtype, causal, reuse=True, **kw)
+        got_n, _ = run_case(B, QH, KH, QL, KL, 64, dtype, causal, reuse=False, **kw)
+        for name in got_r:
+            if name != "dq":
+                assert np.array_equal(got_r[name], got_n[name], equal_nan=True), name
+        check(got_r, want, dtype, tag=f"QL={QL} KL={KL} causal={causal}")
+
+
+def test_attention_pair_neg_inf_entries():
+    """−Inf pair entries scattered through rows that keep finite scores: each
+    such logit is masked exactly (probability 0, dpair 0), as in the
+    reference, on the tensor-core path whose pair bias goes through an
+    identity UMMA."""
+    def pair_fn(pair, rng):
+        pair[rng.random(pair.shape) < 0.2] = -np.inf
+        pair[:, 0, :, :] = 0.0   # key 0 stays finite for every query
+    for dtype in ("bf16", "f16", "f32"):
+        for causal in (False, True):
+            got, want = run_case(2, 4, 4, 200, 200, 64, dtype, causal, True, False, seed=21, pair_fn=pair_fn)
+            check(got, want, dtype, tag=f"causal={causal}")
+
+
+def test_attention_autograd_pair_bf16():
+    """flash_attention under autograd (the rrule: forward keeps its workspace,
+    the pullback reuses the pair tiles) against the oracle."""
+    import nnop
+    import torch
+    rng = np.random.default_rng(77)
+    B, H, L, E = 2, 4, 300, 64
+    q, k, v, do = (rng.standard_normal((B, H, L, E)).astype(np.float32) for _ in range(4))
+    pair = rng.standard_normal((B, L, L, H)).astype(np.float32)
+    ts = [to_dev(a, "bf16").requires_grad_(True) for a in (q, k, v, pair)]
+    o = nnop.flash_attention(*ts[:3], ts[3], causal=True)
+    o.backward(to_dev(do, "bf16"))
+    torch.cuda.synchronize()
+    qr, kr, vr, pr = (to_np(t.detach()) for t in ts)
+    dor = to_np(to_dev(do, "bf16"))
+    scale = orc.attention_scale(E, "bf16")
+    o_o, lse_o = orc.attention_fwd(qr, kr, vr, pr, causal=True, scale=scale)
+    grads = orc.attention_bwd(dor, qr, kr, vr, pr, causal=True, scale=scale)
+    got = dict(o=to_np(o.detach()), dq=to_np(ts[0].grad), dk=to_np(ts[1].grad), dv=to_np(ts[2].grad),
+               dpair=to_np(ts[3].grad))
+    want = dict(o=o_o, dq=grads[0], dk=grads[1], dv=grads[2], dpair=grads[3])
+    check(got, want, "bf16")
