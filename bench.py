@@ -354,7 +354,7 @@ def run_ours(args):
             "config": {"workload": "config2: flash_attention fwd+bwd bf16 causal + pair bias", "E": E, "L": L,
                        "H": H, "B_per_gpu": B, "global_batch": B * world, "causal": causal,
                        "parallelism": f"dp{world} (batch shards, no collective)",
-                       "l2": "inputs larger than L2 (pair 4.29 GB per GPU)"},
+                       "l2": f"inputs larger than L2 (pair {B * L * L * H * 2 / 1e9:.2f} GB per GPU)"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
             # per step: pair_tiles, fa_fwd; preprocess, fa_bwd, dq convert, dpair_from_tiles
@@ -377,7 +377,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch override, for small profiler captures (the headline uses 8)")
     args = ap.parse_args()
+    if args.batch is not None:
+        CFG["B"] = args.batch
     if args.impl == "reference":
         run_reference(args)
     else:

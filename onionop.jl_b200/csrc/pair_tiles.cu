@@ -170,6 +170,171 @@ __global__ void __launch_bounds__(kTB) dpair_from_tiles_kernel(const T* __restri
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// Fast path for H = 8·CQ heads, CQ in {1, 2, 4, 8}: the block's key rows sit in
+// shared memory as 16-byte chunks (CQ per query), chunk L of a row stored at
+// swz(L); a thread moves two heads × 8 queries at a time with 32-bit shared
+// accesses and byte permutes.  The swizzle spreads the 8/CQ query pieces a
+// warp touches at once over distinct bank groups, so neither the 16-byte
+// fills nor the 32-bit gathers conflict.
+template <int CQ>
+__device__ __forceinline__ int swz(int L) {
+    constexpr int NV = 8 / CQ;
+    return L ^ (((L / (8 * CQ)) % NV) * CQ);
+}
+
+// −Inf -> most negative finite on two packed 16-bit values (NaN kept)
+template <typename T>
+__device__ __forceinline__ uint32_t finite2(uint32_t x);
+template <>
+__device__ __forceinline__ uint32_t finite2<__nv_bfloat16>(uint32_t x) {
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&x);
+    const uint32_t lo = 0xFF7FFF7Fu;
+    v = __hmax2_nan(v, *reinterpret_cast<const __nv_bfloat162*>(&lo));
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t finite2<__half>(uint32_t x) {
+    __half2 v = *reinterpret_cast<__half2*>(&x);
+    const uint32_t lo = 0xFBFFFBFFu;
+    v = __hmax2_nan(v, *reinterpret_cast<const __half2*>(&lo));
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T, int CQ>
+__global__ void __launch_bounds__(kTB, 3) pair_tiles_fast_kernel(const T* __restrict__ pair, T* __restrict__ out,
+                                                              const int* __restrict__ kv_len, int64_t QL,
+                                                              int64_t KL, int64_t qlp, int64_t klp, int causal) {
+    constexpr int H = 8 * CQ;
+    constexpr int RC = kTile * CQ;   // 16-byte chunks per key row
+    extern __shared__ __align__(16) uint8_t sm_raw[];
+    uint4* s4 = reinterpret_cast<uint4*>(sm_raw);          // [8][RC] swizzled
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm_raw);
+    const int c = blockIdx.x;
+    const int64_t g = blockIdx.y;
+    const int b = blockIdx.z;
+    if (!visited(c, g, b, kv_len, causal)) return;
+    const int64_t i0 = (int64_t)c * kTile;
+    const int64_t rs = QL * H;
+    const T* src = pair + (((int64_t)b * KL + g * kKeys) * QL + i0) * H;
+    if (g * kKeys + kKeys <= KL && i0 + kTile <= QL && aligned_rows(pair, rs)) {
+#pragma unroll
+        for (int L0 = 0; L0 < RC; L0 += kTB) {
+            const int L = L0 + threadIdx.x;
+            if (RC % kTB == 0 || L < RC) {
+                uint4 u[kKeys];
+#pragma unroll
+                for (int e = 0; e < kKeys; ++e) u[e] = __ldcs(reinterpret_cast<const uint4*>(src + e * rs) + L);
+#pragma unroll
+                for (int e = 0; e < kKeys; ++e) s4[e * RC + swz<CQ>(L)] = u[e];
+            }
+        }
+    } else {
+        uint16_t* s16 = reinterpret_cast<uint16_t*>(sm_raw);
+        for (int e = 0; e < kKeys; ++e) {
+            const bool key_ok = g * kKeys + e < KL;
+            for (int x = threadIdx.x; x < kTile * H; x += kTB) {
+                const bool ok = key_ok && i0 + x / H < QL;
+                const T val = ok ? src[e * rs + x] : from_f<T>(0.f);
+                s16[(e * RC + swz<CQ>(x / 8)) * 8 + x % 8] = *reinterpret_cast<const uint16_t*>(&val);
+            }
+        }
+    }
+    __syncthreads();
+    // thread -> (key kk, 8-query piece v, head pair hp), head pairs fastest
+    constexpr int kPieces = kKeys * (kTile / 8) * (H / 2);
+#pragma unroll 2
+    for (int x = threadIdx.x; x < kPieces; x += kTB) {
+        const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = s32[(kk * RC + swz<CQ>((v * 8 + e) * CQ + hp / 4)) * 4 + hp % 4];
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            lo[j] = finite2<T>(__byte_perm(w[2 * j], w[2 * j + 1], 0x5410));
+            hi[j] = finite2<T>(__byte_perm(w[2 * j], w[2 * j + 1], 0x7632));
+        }
+        T* dst = out + (((int64_t)b * H + 2 * hp) * klp + g * kKeys + kk) * qlp + i0 + v * 8;
+        __stcs(reinterpret_cast<uint4*>(dst), make_uint4(lo[0], lo[1], lo[2], lo[3]));
+        __stcs(reinterpret_cast<uint4*>(dst + klp * qlp), make_uint4(hi[0], hi[1], hi[2], hi[3]));
+    }
+}
+
+template <typename T, int CQ>
+__global__ void __launch_bounds__(kTB, 3) dpair_from_tiles_fast_kernel(const T* __restrict__ tiles,
+                                                                    T* __restrict__ dpair,
+                                                                    const int* __restrict__ kv_len, int64_t QL,
+                                                                    int64_t KL, int64_t qlp, int64_t klp,
+                                                                    int causal) {
+    constexpr int H = 8 * CQ;
+    constexpr int RC = kTile * CQ;
+    extern __shared__ __align__(16) uint8_t sm_raw[];
+    uint4* s4 = reinterpret_cast<uint4*>(sm_raw);
+    uint32_t* s32 = reinterpret_cast<uint32_t*>(sm_raw);
+    const int c = blockIdx.x;
+    const int64_t g = blockIdx.y;
+    const int b = blockIdx.z;
+    const int64_t i0 = (int64_t)c * kTile;
+    const bool vis = visited(c, g, b, kv_len, causal);
+    if (vis) {
+        constexpr int kPieces = kKeys * (kTile / 8) * (H / 2);
+        constexpr int kBatch = 4;   // pieces in flight per thread
+#pragma unroll 1
+        for (int x0 = 0; x0 < kPieces; x0 += kBatch * kTB) {
+            uint4 a[kBatch], bq[kBatch];
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) {
+                const int x = x0 + t * kTB + threadIdx.x;
+                if (x < kPieces) {
+                    const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
+                    const T* p0 = tiles + (((int64_t)b * H + 2 * hp) * klp + g * kKeys + kk) * qlp + i0 + v * 8;
+                    a[t] = __ldcs(reinterpret_cast<const uint4*>(p0));
+                    bq[t] = __ldcs(reinterpret_cast<const uint4*>(p0 + klp * qlp));
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) {
+                const int x = x0 + t * kTB + threadIdx.x;
+                if (x < kPieces) {
+                    const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
+                    const uint32_t aw[4] = {a[t].x, a[t].y, a[t].z, a[t].w};
+                    const uint32_t bw[4] = {bq[t].x, bq[t].y, bq[t].z, bq[t].w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        s32[(kk * RC + swz<CQ>((v * 8 + e) * CQ + hp / 4)) * 4 + hp % 4] =
+                            __byte_perm(aw[e / 2], bw[e / 2], (e & 1) ? 0x7632 : 0x5410);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    const int64_t rs = QL * H;
+    T* dst0 = dpair + (((int64_t)b * KL + g * kKeys) * QL + i0) * H;
+    if (g * kKeys + kKeys <= KL && i0 + kTile <= QL && aligned_rows(dpair, rs)) {
+#pragma unroll
+        for (int L0 = 0; L0 < RC; L0 += kTB) {
+            const int L = L0 + threadIdx.x;
+            if (RC % kTB == 0 || L < RC) {
+#pragma unroll
+                for (int kk = 0; kk < kKeys; ++kk) {
+                    const uint4 u = vis ? s4[kk * RC + swz<CQ>(L)] : make_uint4(0, 0, 0, 0);
+                    __stcs(reinterpret_cast<uint4*>(dst0 + kk * rs) + L, u);
+                }
+            }
+        }
+    } else {
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(sm_raw);
+        const int n = (int)((i0 + kTile <= QL ? kTile : QL - i0) * H);
+        for (int kk = 0; kk < kKeys && g * kKeys + kk < KL; ++kk)
+            for (int x = threadIdx.x; x < n; x += kTB) {
+                const uint16_t bits = vis ? s16[(kk * RC + swz<CQ>(x / 8)) * 8 + x % 8] : (uint16_t)0;
+                dst0[kk * rs + x] = *reinterpret_cast<const T*>(&bits);
+            }
+    }
+}
+
 template <typename KernelT>
 int set_smem(KernelT kern, size_t smem, const char* what) {
     if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -192,10 +357,27 @@ int launch_pair_tiles(const T* pair, T* out, const int* kv_len, int64_t QL, int6
                       cudaStream_t s) {
     const int64_t qlp = pad_tile(QL), klp = pad_tile(KL);
     const size_t smem = (size_t)kKeys * kTile * H * sizeof(T);
-    int st = set_smem(pair_tiles_kernel<T>, smem, "pair_tiles");
-    if (st) return st;
     dim3 grid((unsigned)(qlp / kTile), (unsigned)(klp / kKeys), B);
-    pair_tiles_kernel<T><<<grid, kTB, smem, s>>>(pair, out, kv_len, QL, KL, H, qlp, klp, causal ? 1 : 0);
+    const int cz = causal ? 1 : 0;
+    int st = NNOP_OK;
+#define NNOP_TILES_FAST(CQ)                                                                              \
+    case 8 * CQ:                                                                                          \
+        st = set_smem(pair_tiles_fast_kernel<T, CQ>, smem, "pair_tiles");                               \
+        if (st) return st;                                                                                \
+        pair_tiles_fast_kernel<T, CQ><<<grid, kTB, smem, s>>>(pair, out, kv_len, QL, KL, qlp, klp, cz); \
+        return check_launch("pair_tiles");
+    switch (H) {
+        NNOP_TILES_FAST(1)
+        NNOP_TILES_FAST(2)
+        NNOP_TILES_FAST(4)
+        NNOP_TILES_FAST(8)
+        default:
+            break;
+    }
+#undef NNOP_TILES_FAST
+    st = set_smem(pair_tiles_kernel<T>, smem, "pair_tiles");
+    if (st) return st;
+    pair_tiles_kernel<T><<<grid, kTB, smem, s>>>(pair, out, kv_len, QL, KL, H, qlp, klp, cz);
     return check_launch("pair_tiles");
 }
 
@@ -204,10 +386,27 @@ int launch_dpair_from_tiles(const T* tiles, T* dpair, const int* kv_len, int64_t
                             bool causal, cudaStream_t s) {
     const int64_t qlp = pad_tile(QL), klp = pad_tile(KL);
     const size_t smem = (size_t)kKeys * kTile * H * sizeof(T);
-    int st = set_smem(dpair_from_tiles_kernel<T>, smem, "dpair_from_tiles");
-    if (st) return st;
     dim3 grid((unsigned)(qlp / kTile), (unsigned)(klp / kKeys), B);
-    dpair_from_tiles_kernel<T><<<grid, kTB, smem, s>>>(tiles, dpair, kv_len, QL, KL, H, qlp, klp, causal ? 1 : 0);
+    const int cz = causal ? 1 : 0;
+    int st = NNOP_OK;
+#define NNOP_DPAIR_FAST(CQ)                                                                                    \
+    case 8 * CQ:                                                                                                \
+        st = set_smem(dpair_from_tiles_fast_kernel<T, CQ>, smem, "dpair_from_tiles");                         \
+        if (st) return st;                                                                                      \
+        dpair_from_tiles_fast_kernel<T, CQ><<<grid, kTB, smem, s>>>(tiles, dpair, kv_len, QL, KL, qlp, klp, cz); \
+        return check_launch("dpair_from_tiles");
+    switch (H) {
+        NNOP_DPAIR_FAST(1)
+        NNOP_DPAIR_FAST(2)
+        NNOP_DPAIR_FAST(4)
+        NNOP_DPAIR_FAST(8)
+        default:
+            break;
+    }
+#undef NNOP_DPAIR_FAST
+    st = set_smem(dpair_from_tiles_kernel<T>, smem, "dpair_from_tiles");
+    if (st) return st;
+    dpair_from_tiles_kernel<T><<<grid, kTB, smem, s>>>(tiles, dpair, kv_len, QL, KL, H, qlp, klp, cz);
     return check_launch("dpair_from_tiles");
 }
 
