@@ -6,14 +6,18 @@
 // five WMMA/SIMT GEMMs, a read-modify-write of dq in global memory and atomics
 // for GQA.  Here one CTA owns a 128-key tile of one KV head of one batch and
 // walks the 128-query tiles of every query head of its GQA group; dK and dV
-// stay in TMEM for the whole walk.  Per step (query tile i):
-//   Sᵀ  = K·Q_iᵀ (+ c·I·pairᵀ)  (keys on TMEM lanes)   UMMA ss
-//   dPᵀ = V·dO_iᵀ                                       UMMA ss
-//   Pᵀ  = exp(Sᵀ·scale − lse_i),  dSᵀ = Pᵀ∘(dPᵀ − δ_i)   (elementwise)
-//   dV += Pᵀ·dO_i   (Pᵀ from TMEM)                      UMMA ts
-//   dK += dSᵀ·Q_i   (dSᵀ from TMEM)                     UMMA ts
-//   dQ_i = dS·K     (dS from shared memory, MN-major)   UMMA ss
-//   dq_acc[i] += scale·dQ_i  (fp32 vector reductions, red.global.add.v4.f32)
+// stay in TMEM for the whole walk.  Each query tile is processed as two
+// 64-query halves, half hf by elementwise warpgroup hf, each with its own
+// TMEM score buffers, so the tensor cores work on one half while the other
+// half's exponentials run.  Per tile t and half hf:
+//   Sᵀ  = K·Q_hfᵀ (+ c·I·pairᵀ)  (keys on TMEM lanes)   UMMA ss
+//   dPᵀ = V·dO_hfᵀ                                       UMMA ss
+//   Pᵀ  = exp(Sᵀ·scale − lse),  dSᵀ = Pᵀ∘(dPᵀ − δ)       (elementwise)
+//   dV += Pᵀ·dO_hf   (Pᵀ from TMEM)                      UMMA ts
+//   dK += dSᵀ·Q_hf   (dSᵀ from TMEM)                     UMMA ts
+// and per tile: dQ_t = dS·K (dS from shared memory, MN-major, double
+// buffered so the next tile's dS can be written meanwhile), then
+// dq_acc[t] += scale·dQ_t (fp32 vector reductions, red.global.add.v4.f32).
 //   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
 //                 written per head as key-major dS tiles, see pair_tiles.cu.
 // The pair bias enters through the tensor cores: c = 1/scale (a power of two,
@@ -21,19 +25,18 @@
 // fa_sm100.cuh as A, the pair tile [key][query] of the key-major per-head copy
 // pair_tiles() writes as the MN-major B operand.
 // Warp roles (512 threads):
-//   warp 0      TMA producer (K, V once; Q_i, dO_i into a 2-stage ring)
+//   warp 0      TMA producer (K, V once; Q_t, dO_t into a 2-stage ring; the
+//               pair tile of (query tile, key tile, head), two 64-query boxes)
 //   warp 1      MMA issuer (one lane)
-//   warps 2-3   tile provider: lse_i (log2 units) and δ_i
-//   (the pair tile of (query tile, key tile, head), two 64-query boxes of
-//   [B][H][KL][QL], is also loaded by warp 0; dS goes out as 32-byte row
-//   pieces in the same layout and dpair_from_tiles() turns it into dpair)
-//   warps 4-11  elementwise: two warpgroups on the same 128 TMEM lanes
-//               (one key per lane), query columns [0,64) and [64,128)
+//   warps 2-3   tile provider: lse (log2 units) and δ of the tile's queries
+//   warps 4-7   elementwise, query half 0 (one key per TMEM lane)
+//   warps 8-11  elementwise, query half 1
 //   warps 12-15 dQ: TMEM dQ rows -> fp32 reductions into the accumulator
-// TMEM columns: Sᵀ [0,128), dPᵀ [128,256), dV [256,320), dK [320,384),
-// dQ [384,448).  The 16-bit Pᵀ / dSᵀ overwrite their own warpgroup's score
-// columns (query c -> column c/2 + 32·[c >= 64]) so neither warpgroup can
-// overwrite scores the other has not read yet.  All mbarrier waits are bounded.
+// TMEM columns: Sᵀ half 0 [0,64), half 1 [64,128), dPᵀ half 0 [128,192),
+// half 1 [192,256), dV [256,320), dK [320,384), dQ [384,448).  The 16-bit
+// Pᵀ / dSᵀ of a half overwrite the first 32 columns of its own score buffers.
+// All mbarrier waits are bounded; a wait that gives up records its site
+// (0-14) in the timeout flags and the CTA leaves.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -50,24 +53,26 @@ namespace {
 using namespace sm100;
 
 constexpr int kBN = 128;   // keys per CTA (TMEM lanes)
-constexpr int kBM = 128;   // queries per step
+constexpr int kBM = 128;   // queries per tile
+constexpr int kHM = 64;    // queries per half
 constexpr int kE = 64;
 constexpr int kThreads = 512;
 
 enum Bar {
     kKVFull = 0,
-    kQFull = 1,       // +stage: Q_i and dO_i landed
-    kQEmpty = 3,      // +stage: dV/dK MMAs of the step retired
-    kSFull = 5,       // Sᵀ, dPᵀ in TMEM
-    kPFull = 6,       // elementwise done (256 arrivals)
-    kDQFull = 7,      // dQ_i in TMEM
-    kDQEmpty = 8,     // dQ warps done with TMEM dQ (128 arrivals)
-    kTileFull = 9,    // +buffer: provider -> elementwise (64 arrivals)
-    kTileEmpty = 11,  // +buffer: elementwise -> provider (256 arrivals)
-    kFinal = 13,      // every MMA retired
-    kPairFull = 14,   // +buffer: pair tile landed (TMA)
-    kPairEmpty = 16,  // +buffer: its UMMAs retired
-    kNumBars = 18
+    kQFull = 1,       // +stage: Q_t and dO_t landed
+    kQEmpty = 3,      // +stage: dV/dK MMAs of the tile retired
+    kSFull = 5,       // +half: Sᵀ, dPᵀ of the half in TMEM
+    kPFull = 7,       // +half: elementwise done with the half (128 arrivals)
+    kDSEmpty = 9,     // +buffer: dQ MMA done reading the dS buffer
+    kDQFull = 11,     // dQ_t in TMEM
+    kDQEmpty = 12,    // dQ warps done with TMEM dQ (128 arrivals)
+    kTileFull = 13,   // +buffer: provider -> elementwise (64 arrivals)
+    kTileEmpty = 15,  // +buffer: elementwise -> provider (256 arrivals)
+    kFinal = 17,      // every MMA retired
+    kPairFull = 18,   // pair tile landed (TMA)
+    kPairEmpty = 19,  // its UMMAs retired
+    kNumBars = 20
 };
 
 struct Lay {
@@ -76,17 +81,19 @@ struct Lay {
     static constexpr int kV = kK + kTile;
     static constexpr int kQ = kV + kTile;           // 2 stages
     static constexpr int kDO = kQ + 2 * kTile;      // 2 stages
-    static constexpr int kDS = kDO + 2 * kTile;     // [2 halves][128 keys][64 queries], MN-major SW128
-    static constexpr int kPair = kDS + 2 * kTile;   // 2 buffers of [2 halves][BN keys][64 queries] SW128
+    static constexpr int kDS = kDO + 2 * kTile;     // 2 buffers of [2 halves][128 keys][64 queries], MN-major SW128
+    static constexpr int kDSBytes = 2 * kTile;
+    static constexpr int kPair = kDS + 2 * kDSBytes;   // [2 halves][BN keys][64 queries] SW128
     static constexpr int kPairBytes = kBM * kBN * 2;
-    static constexpr int kEye = kPair + 2 * kPairBytes;   // shifted identity (1024-aligned)
-    static constexpr int kLse = kEye + kEyeBytes;         // [2][BM] float (log2 units)
-    static constexpr int kDel = kLse + 2 * kBM * 4;       // [2][BM] float
+    static constexpr int kEye = kPair + kPairBytes;     // shifted identity (1024-aligned)
+    static constexpr int kLse = kEye + kEyeBytes;       // [2][BM] float (log2 units)
+    static constexpr int kDel = kLse + 2 * kBM * 4;     // [2][BM] float
     static constexpr int kBar = kDel + 2 * kBM * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kTotal = kTmemSlot + 16;
     static constexpr int kAlloc = kTotal + 1024;
 };
+static_assert(Lay::kAlloc <= 227 * 1024, "shared memory");
 
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
     asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
@@ -97,6 +104,29 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* ab, int site) {
     const bool ok = wait(bar, parity, ab, site);
     return __all_sync(0xffffffffu, ok);
+}
+
+// 16 columns of Pᵀ and dSᵀ from 16 columns of Sᵀ and dPᵀ; columns t outside
+// [lo, hi) are masked (probability 0).
+template <typename T, bool MASKED>
+__device__ __forceinline__ void elementwise16(const uint32_t (&sr)[16], const uint32_t (&dr)[16],
+                                              const float4 (&l4)[4], const float4 (&d4)[4], float sl2, int lo,
+                                              int hi, uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+    const float* lse = reinterpret_cast<const float*>(l4);
+    const float* del = reinterpret_cast<const float*>(d4);
+#pragma unroll
+    for (int t = 0; t < 16; t += 2) {
+        float pv[2], dv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float pr = ex2(fmaf(__uint_as_float(sr[t + u]), sl2, -lse[t + u]));
+            if (MASKED) pr = (t + u >= lo && t + u < hi) ? pr : 0.f;
+            pv[u] = pr;
+            dv[u] = pr * (__uint_as_float(dr[t + u]) - del[t + u]);
+        }
+        pk[t >> 1] = pack16<T>(pv[0], pv[1]);
+        dk[t >> 1] = pack16<T>(dv[0], dv[1]);
+    }
 }
 
 template <typename T, bool CAUSAL, bool PAIR, bool MASK>
@@ -122,7 +152,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int n_qt = (int)((QL + kBM - 1) / kBM);
     const int qt0 = CAUSAL ? (int)(k0 / kBM) : 0;
     const int nq = (k0 < kv_len && qt0 < n_qt) ? n_qt - qt0 : 0;
-    const int steps = nq * p.n_rep;
+    const int tiles = nq * p.n_rep;
 
     __shared__ int s_abort;   // set by the first wait of this CTA that gives up
     volatile int* ab = &s_abort;
@@ -132,16 +162,17 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars[kQFull + s], 1);
             mbar_init(&bars[kQEmpty + s], 1);
+            mbar_init(&bars[kSFull + s], 1);
+            mbar_init(&bars[kPFull + s], 128);
+            mbar_init(&bars[kDSEmpty + s], 1);
             mbar_init(&bars[kTileFull + s], 64);
             mbar_init(&bars[kTileEmpty + s], 256);
-            mbar_init(&bars[kPairFull + s], 1);
-            mbar_init(&bars[kPairEmpty + s], 1);
         }
-        mbar_init(&bars[kSFull], 1);
-        mbar_init(&bars[kPFull], 256);
         mbar_init(&bars[kDQFull], 1);
         mbar_init(&bars[kDQEmpty], 128);
         mbar_init(&bars[kFinal], 1);
+        mbar_init(&bars[kPairFull], 1);
+        mbar_init(&bars[kPairEmpty], 1);
         fence_mbar_init();
     }
     if (PAIR) {
@@ -160,7 +191,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
-        if (lane == 0 && steps > 0) {
+        if (lane == 0 && tiles > 0) {
             tma_prefetch(&tm_q);
             tma_prefetch(&tm_k);
             tma_prefetch(&tm_v);
@@ -170,89 +201,105 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             mbar_expect_tx(&bars[kKVFull], 2 * Lay::kTile);
             tma_load_3d(smem + Lay::kK, &tm_k, &bars[kKVFull], 0, (int)k0, bh_k);
             tma_load_3d(smem + Lay::kV, &tm_v, &bars[kKVFull], 0, (int)k0, bh_k);
-            int issued = 0;
-            for (int st = 0; st < steps; ++st) {
-                const int s = st & 1;
-                if (st >= 2 && !wait(&bars[kQEmpty + s], ((st >> 1) - 1) & 1, ab, 1)) break;
-                if (PAIR && st >= 2 && !wait(&bars[kPairEmpty + s], ((st >> 1) - 1) & 1, ab, 14)) break;
-                issued = st + 1;
-                const int h = kvh * p.n_rep + st / nq;
-                const int q0 = (qt0 + st % nq) * kBM;
+            int issued = 0, pair_issued = 0;
+            for (int t = 0; t < tiles; ++t) {
+                const int s = t & 1;
+                if (t >= 2 && !wait(&bars[kQEmpty + s], ((t >> 1) - 1) & 1, ab, 0)) break;
+                const int h = kvh * p.n_rep + t / nq;
+                const int q0 = (qt0 + t % nq) * kBM;
                 mbar_expect_tx(&bars[kQFull + s], 2 * Lay::kTile);
                 tma_load_3d(smem + Lay::kQ + s * Lay::kTile, &tm_q, &bars[kQFull + s], 0, q0, b * QH + h);
                 tma_load_3d(smem + Lay::kDO + s * Lay::kTile, &tm_do, &bars[kQFull + s], 0, q0, b * QH + h);
+                issued = t + 1;
                 if (PAIR) {
-                    mbar_expect_tx(&bars[kPairFull + s], Lay::kPairBytes);
+                    if (t >= 1 && !wait(&bars[kPairEmpty], (t - 1) & 1, ab, 1)) break;
+                    mbar_expect_tx(&bars[kPairFull], Lay::kPairBytes);
 #pragma unroll
                     for (int half = 0; half < 2; ++half)
-                        tma_load_3d(smem + Lay::kPair + s * Lay::kPairBytes + half * kBN * 128, &tm_pair,
-                                    &bars[kPairFull + s], q0 + half * 64, (int)k0, b * QH + h);
+                        tma_load_3d(smem + Lay::kPair + half * kBN * 128, &tm_pair, &bars[kPairFull],
+                                    q0 + half * kHM, (int)k0, b * QH + h);
+                    pair_issued = t + 1;
                 }
             }
             // copies in flight land before the CTA leaves (bounded waits)
             wait(&bars[kKVFull], 0, ab, 2);
-            for (int st = issued - 2 < 0 ? 0 : issued - 2; st < issued; ++st) {
-                wait(&bars[kQFull + (st & 1)], (st >> 1) & 1, ab, 3);
-                if (PAIR) wait(&bars[kPairFull + (st & 1)], (st >> 1) & 1, ab, 15);
-            }
+            for (int t = issued - 2 < 0 ? 0 : issued - 2; t < issued; ++t)
+                wait(&bars[kQFull + (t & 1)], (t >> 1) & 1, ab, 2);
+            if (PAIR && pair_issued > 0) wait(&bars[kPairFull], (pair_issued - 1) & 1, ab, 2);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
-        constexpr uint32_t id_s = idesc_f16<kBF16>(128, 128, false, false);   // Sᵀ, dPᵀ
-        constexpr uint32_t id_kv = idesc_f16<kBF16>(128, 64, false, true);    // dV, dK (A in TMEM)
-        constexpr uint32_t id_q = idesc_f16<kBF16>(128, 64, true, true);      // dQ (A = dS, MN-major)
+        constexpr uint32_t id_s = idesc_f16<kBF16>(128, kHM, false, false);   // Sᵀ, dPᵀ of a half
+        constexpr uint32_t id_p = idesc_f16<kBF16>(128, kHM, false, true);    // Sᵀ += c·I·pairᵀ
+        constexpr uint32_t id_kv = idesc_f16<kBF16>(128, kE, false, true);    // dV, dK (A in TMEM)
+        constexpr uint32_t id_q = idesc_f16<kBF16>(128, kE, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
-        constexpr uint32_t id_p = idesc_f16<kBF16>(128, 128, false, true);   // Sᵀ += c·I·pairᵀ
-        const uint32_t sDS = smem_u32(smem + Lay::kDS);
-        const uint32_t sEye = smem_u32(smem + Lay::kEye);
-        bool ok = steps > 0 && wait_warp(&bars[kKVFull], 0, ab, 4);
-        for (int st = 0; ok && st < steps; ++st) {
-            const int s = st & 1;
-            if (!wait_warp(&bars[kQFull + s], (st >> 1) & 1, ab, 5)) break;
-            if (PAIR && !wait_warp(&bars[kPairFull + s], (st >> 1) & 1, ab, 16)) break;
-            tc_fence_after();
-            const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile);
-            const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile);
+        const uint32_t sEye = smem_u32(smem + Lay::kEye), sP = smem_u32(smem + Lay::kPair);
+        // Sᵀ/dPᵀ (+ pair) of half hf of tile t into the half's TMEM buffers
+        auto issue_s = [&](int t, int hf) -> bool {
+            const int s = t & 1;
+            if (hf == 0) {
+                if (!wait_warp(&bars[kQFull + s], (t >> 1) & 1, ab, 4)) return false;
+                if (PAIR && !wait_warp(&bars[kPairFull], t & 1, ab, 5)) return false;
+                tc_fence_after();
+            }
             if (lane == 0) {
+                const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile) + hf * kHM * 128;
+                const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile) + hf * kHM * 128;
+                const uint32_t dS = tS + hf * kHM, dDP = tDP + hf * kHM;
 #pragma unroll
                 for (int kk = 0; kk < kE / 16; ++kk) {
-                    umma_ss(tS, desc_k_sw128(sK + kk * 32), desc_k_sw128(sQ + kk * 32), id_s, kk > 0 ? 1u : 0u);
-                    umma_ss(tDP, desc_k_sw128(sV + kk * 32), desc_k_sw128(sDO + kk * 32), id_s, kk > 0 ? 1u : 0u);
+                    umma_ss(dS, desc_k_sw128(sK + kk * 32), desc_k_sw128(sQ + kk * 32), id_s, kk > 0 ? 1u : 0u);
+                    umma_ss(dDP, desc_k_sw128(sV + kk * 32), desc_k_sw128(sDO + kk * 32), id_s, kk > 0 ? 1u : 0u);
                 }
                 if (PAIR) {
-                    // B = pair tile [key][query]: MN-major over queries, K = keys
-                    const uint32_t sP = smem_u32(smem + Lay::kPair + s * Lay::kPairBytes);
+                    // B = pair half [key][64 queries]: MN-major over queries, K = keys
 #pragma unroll
                     for (int kk = 0; kk < kBN / 16; ++kk)
-                        umma_ss(tS, desc_k_sw128(eye_step(sEye, kk)), desc_mn_sw128(sP + kk * 16 * 128, kBN * 128),
-                                id_p, 1u);
-                    umma_commit(&bars[kPairEmpty + s]);
+                        umma_ss(dS, desc_k_sw128(eye_step(sEye, kk)),
+                                desc_mn_sw128(sP + hf * kBN * 128 + kk * 16 * 128, 0), id_p, 1u);
+                    if (hf == 1) umma_commit(&bars[kPairEmpty]);
                 }
-                umma_commit(&bars[kSFull]);
+                umma_commit(&bars[kSFull + hf]);
             }
             __syncwarp();
-            if (!wait_warp(&bars[kPFull], st & 1, ab, 6)) break;
-            tc_fence_after();
-            if (lane == 0) {
+            return true;
+        };
+        bool ok = tiles > 0 && wait_warp(&bars[kKVFull], 0, ab, 3);
+        if (ok) ok = issue_s(0, 0) && issue_s(0, 1);
+        for (int t = 0; ok && t < tiles; ++t) {
+            const int s = t & 1;
+            for (int hf = 0; hf < 2; ++hf) {
+                if (!wait_warp(&bars[kPFull + hf], t & 1, ab, 6)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile) + hf * kHM * 128;
+                    const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile) + hf * kHM * 128;
 #pragma unroll
-                for (int kk = 0; kk < kBM / 16; ++kk) {
-                    // packed 16-bit Pᵀ/dSᵀ of queries [16kk, 16kk+16)
-                    const uint32_t pcol = kk * 8 + (kk >= 4 ? 32 : 0);
-                    const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
-                    umma_ts(tDV, tS + pcol, desc_mn_sw128(sDO + kk * 16 * 128, 0), id_kv, acc);
-                    umma_ts(tDK, tDP + pcol, desc_mn_sw128(sQ + kk * 16 * 128, 0), id_kv, acc);
+                    for (int kk = 0; kk < kHM / 16; ++kk) {
+                        // packed 16-bit Pᵀ/dSᵀ of the half's queries [16kk, 16kk+16)
+                        const uint32_t pcol = hf * kHM + kk * 8;
+                        const uint32_t acc = (t > 0 || hf > 0 || kk > 0) ? 1u : 0u;
+                        umma_ts(tDV, tS + pcol, desc_mn_sw128(sDO + kk * 16 * 128, 0), id_kv, acc);
+                        umma_ts(tDK, tDP + pcol, desc_mn_sw128(sQ + kk * 16 * 128, 0), id_kv, acc);
+                    }
+                    if (hf == 1) umma_commit(&bars[kQEmpty + s]);
                 }
-                umma_commit(&bars[kQEmpty + s]);
+                __syncwarp();
+                if (t + 1 < tiles && !issue_s(t + 1, hf)) { ok = false; break; }
             }
-            __syncwarp();
-            if (st > 0 && !wait_warp(&bars[kDQEmpty], (st - 1) & 1, ab, 7)) break;
+            if (!ok) break;
+            // dQ_t = dS_t·K once the previous dQ has been drained from TMEM
+            if (t > 0 && !wait_warp(&bars[kDQEmpty], (t - 1) & 1, ab, 7)) break;
             tc_fence_after();
             if (lane == 0) {
+                const uint32_t sDS = smem_u32(smem + Lay::kDS + s * Lay::kDSBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk)
-                    umma_ss(tDQ, desc_mn_sw128(sDS + kk * 16 * 128, 128 * 128), desc_mn_sw128(sK + kk * 16 * 128, 0),
+                    umma_ss(tDQ, desc_mn_sw128(sDS + kk * 16 * 128, kBN * 128), desc_mn_sw128(sK + kk * 16 * 128, 0),
                             id_q, kk > 0 ? 1u : 0u);
                 umma_commit(&bars[kDQFull]);
+                umma_commit(&bars[kDSEmpty + s]);
             }
             __syncwarp();
         }
@@ -263,74 +310,75 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     } else if (warp < 4) {
         // ------------------------------------------------------ tile provider
         const int tp = threadIdx.x - 64;
-        for (int st = 0; st < steps; ++st) {
-            const int buf = st & 1;
-            if (st >= 2 && !wait(&bars[kTileEmpty + buf], ((st >> 1) - 1) & 1, ab, 9)) break;
-            const int h = kvh * p.n_rep + st / nq;
-            const int64_t q0 = (int64_t)(qt0 + st % nq) * kBM;
+        for (int t = 0; t < tiles; ++t) {
+            const int buf = t & 1;
+            if (t >= 2 && !wait(&bars[kTileEmpty + buf], ((t >> 1) - 1) & 1, ab, 9)) break;
+            const int h = kvh * p.n_rep + t / nq;
+            const int64_t q0 = (int64_t)(qt0 + t % nq) * kBM;
             const int64_t ro = ((int64_t)b * QH + h) * QL;
-            for (int t = tp; t < kBM; t += 64) {
-                const int64_t i = q0 + t;
-                sLse[buf * kBM + t] = i < QL ? p.lse[ro + i] * kLog2e : 0.f;
-                sDel[buf * kBM + t] = i < QL ? p.delta[ro + i] : 0.f;
+            for (int u = tp; u < kBM; u += 64) {
+                const int64_t i = q0 + u;
+                sLse[buf * kBM + u] = i < QL ? p.lse[ro + i] * kLog2e : 0.f;
+                sDel[buf * kBM + u] = i < QL ? p.delta[ro + i] : 0.f;
             }
             mbar_arrive(&bars[kTileFull + buf]);
         }
     } else if (warp < 12) {
         // ------------------------------------------------------ elementwise
         const int jr = (threadIdx.x - 128) & 127;            // key row = TMEM lane
-        const int c0 = ((threadIdx.x - 128) >> 7) * 64;       // query columns [c0, c0+64)
+        const int hf = (threadIdx.x - 128) >> 7;             // query half
         const int64_t j = k0 + jr;
         bool key_ok = j < KL;
         if (MASK && key_ok) key_ok = p.kmask[(int64_t)b * KL + j] != 0;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tSh = tS + hf * kHM + lane_off, tDPh = tDP + hf * kHM + lane_off;
         const float sl2 = p.scale * kLog2e;
-        uint8_t* sDS = smem + Lay::kDS;
-        for (int st = 0; st < steps; ++st) {
-            const int buf = st & 1;
-            const int h = kvh * p.n_rep + st / nq;
-            const int64_t q0 = (int64_t)(qt0 + st % nq) * kBM;
-            if (!wait_warp(&bars[kTileFull + buf], (st >> 1) & 1, ab, 10)) break;
-            if (!wait_warp(&bars[kSFull], st & 1, ab, 11)) break;
+        for (int t = 0; t < tiles; ++t) {
+            const int buf = t & 1;
+            const int h = kvh * p.n_rep + t / nq;
+            const int64_t qh0 = (int64_t)(qt0 + t % nq) * kBM + hf * kHM;   // first query of the half
+            if (!wait_warp(&bars[kTileFull + buf], (t >> 1) & 1, ab, 10)) break;
+            if (!wait_warp(&bars[kSFull + hf], t & 1, ab, 11)) break;
+            if (t >= 2 && !wait_warp(&bars[kDSEmpty + buf], ((t >> 1) - 1) & 1, ab, 12)) break;
             tc_fence_after();
-            // dS tile row of this key: [b][h][key][query]
-            uint16_t* dst_row = PAIR ? ds_tiles + (((int64_t)b * QH + h) * klp + j) * qlp + q0 : nullptr;
+            // valid query columns of this key within the half: [cmin, cmax)
+            const int64_t nvq = QL - qh0;
+            const int cmax = key_ok ? (int)(nvq < kHM ? (nvq > 0 ? nvq : 0) : kHM) : 0;
+            const int64_t cm = CAUSAL ? j - qh0 : 0;
+            const int cmin = (int)(cm < 0 ? 0 : (cm > kHM ? kHM : cm));
+            // dS row of this key in the per-head tiles: [b][h][key][query]
+            uint16_t* dst_row = PAIR ? ds_tiles + (((int64_t)b * QH + h) * klp + j) * qlp + qh0 : nullptr;
+            uint8_t* sDS = smem + Lay::kDS + buf * Lay::kDSBytes + hf * (kBN * 128) + jr * 128;
+            const float* lse_h = sLse + buf * kBM + hf * kHM;
+            const float* del_h = sDel + buf * kBM + hf * kHM;
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
-                const int col = c0 + cc * 16;
+            for (int cc = 0; cc < kHM / 16; ++cc) {
+                const int col = cc * 16;
                 uint32_t sr[16], dr[16];
-                tmem_ld16(tS + lane_off + col, sr);
-                tmem_ld16(tDP + lane_off + col, dr);
+                tmem_ld16(tSh + col, sr);
+                tmem_ld16(tDPh + col, dr);
+                float4 l4[4], d4[4];
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    l4[v] = reinterpret_cast<const float4*>(lse_h + col)[v];
+                    d4[v] = reinterpret_cast<const float4*>(del_h + col)[v];
+                }
                 tmem_ld_wait();
                 uint32_t pk[8], dk[8];
-#pragma unroll
-                for (int t = 0; t < 16; t += 2) {
-                    float pv[2], dv[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int c = col + t + u;
-                        const int64_t i = q0 + c;
-                        bool valid = key_ok && i < QL;
-                        if (CAUSAL) valid = valid && (j <= i);
-                        const float x = __uint_as_float(sr[t + u]) * sl2 - sLse[buf * kBM + c];
-                        const float pr = valid ? ex2(x) : 0.f;
-                        pv[u] = pr;
-                        dv[u] = pr * (__uint_as_float(dr[t + u]) - sDel[buf * kBM + c]);
-                    }
-                    pk[t >> 1] = pack16<T>(pv[0], pv[1]);
-                    dk[t >> 1] = pack16<T>(dv[0], dv[1]);
-                }
-                const uint32_t pcol = col / 2 + (c0 ? 32 : 0);
-                tmem_st8(tS + lane_off + pcol, pk);
-                tmem_st8(tDP + lane_off + pcol, dk);
+                const int lo = cmin - col, hi = cmax - col;
+                if (lo <= 0 && hi >= 16)
+                    elementwise16<T, false>(sr, dr, l4, d4, sl2, 0, 16, pk, dk);
+                else
+                    elementwise16<T, true>(sr, dr, l4, d4, sl2, lo, hi, pk, dk);
+                tmem_st8(tSh + cc * 8, pk);
+                tmem_st8(tDPh + cc * 8, dk);
                 // dS (16-bit) into shared memory for the dQ MMA: row jr, queries
-                // col..col+15, canonical MN-major 128-byte-swizzle layout.
+                // col..col+15 of the half, canonical MN-major 128-byte swizzle.
 #pragma unroll
                 for (int v = 0; v < 2; ++v) {
-                    const int q8 = col + v * 8;
-                    const int half = q8 >> 6, chunk = (q8 & 63) >> 3;
-                    uint4* dst = reinterpret_cast<uint4*>(sDS + half * (128 * 128) + jr * 128 + ((chunk ^ (jr & 7)) << 4));
-                    *dst = make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]);
+                    const int chunk = cc * 2 + v;
+                    *reinterpret_cast<uint4*>(sDS + ((chunk ^ (jr & 7)) << 4)) =
+                        make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]);
                 }
                 if (PAIR) {
 #pragma unroll
@@ -343,12 +391,12 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             tmem_st_wait();
             fence_proxy_async_smem();   // dS smem writes -> tensor-core (async proxy) reads
             tc_fence_before();
-            mbar_arrive(&bars[kPFull]);
+            mbar_arrive(&bars[kPFull + hf]);
         }
-        // epilogue: dK (warpgroup 0) and dV (warpgroup 1) rows of this CTA's keys
-        if (wait_warp(&bars[kFinal], 0, ab, 12)) {
+        // epilogue: dK (half-0 warpgroup) and dV (half-1 warpgroup) rows of this CTA's keys
+        if (wait_warp(&bars[kFinal], 0, ab, 13)) {
             tc_fence_after();
-            const bool is_dk = c0 == 0;
+            const bool is_dk = hf == 0;
             const uint32_t src = (is_dk ? tDK : tDV) + lane_off;
             T* dst = reinterpret_cast<T*>(is_dk ? p.dk : p.dv) + (((int64_t)b * p.KH + kvh) * KL + j) * kE;
             const float mul = is_dk ? p.scale : 1.f;
@@ -360,8 +408,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 if (j < KL) {
                     uint32_t pk[8];
 #pragma unroll
-                    for (int t = 0; t < 8; ++t)
-                        pk[t] = steps > 0 ? pack16<T>(__uint_as_float(raw[2 * t]) * mul, __uint_as_float(raw[2 * t + 1]) * mul)
+                    for (int u = 0; u < 8; ++u)
+                        pk[u] = tiles > 0 ? pack16<T>(__uint_as_float(raw[2 * u]) * mul, __uint_as_float(raw[2 * u + 1]) * mul)
                                           : 0u;
                     uint4* d4 = reinterpret_cast<uint4*>(dst + c * 16);
                     d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -373,10 +421,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         // ------------------------------------------------------ dQ reductions
         const int r = threadIdx.x - 384;                      // query row = TMEM lane
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        for (int st = 0; st < steps; ++st) {
-            const int h = kvh * p.n_rep + st / nq;
-            const int64_t i = (int64_t)(qt0 + st % nq) * kBM + r;
-            if (!wait_warp(&bars[kDQFull], st & 1, ab, 13)) break;
+        for (int t = 0; t < tiles; ++t) {
+            const int h = kvh * p.n_rep + t / nq;
+            const int64_t i = (int64_t)(qt0 + t % nq) * kBM + r;
+            if (!wait_warp(&bars[kDQFull], t & 1, ab, 14)) break;
             tc_fence_after();
             float* dq = p.dq_acc + (((int64_t)b * QH + h) * QL + i) * kE;
 #pragma unroll
