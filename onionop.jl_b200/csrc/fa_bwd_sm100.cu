@@ -10,9 +10,9 @@
 // 64-query halves, half hf by elementwise warpgroup hf, each with its own
 // TMEM score buffers, so the tensor cores work on one half while the other
 // half's exponentials run.  Per tile t and half hf:
-//   Sᵀ  = K·Q_hfᵀ (+ c·I·pairᵀ)  (keys on TMEM lanes)   UMMA ss
+//   Sᵀ  = K·Q_hfᵀ              (keys on TMEM lanes)     UMMA ss
 //   dPᵀ = V·dO_hfᵀ                                       UMMA ss
-//   Pᵀ  = exp(Sᵀ·scale − lse),  dSᵀ = Pᵀ∘(dPᵀ − δ)       (elementwise)
+//   Pᵀ  = exp(Sᵀ·scale + pairᵀ − lse),  dSᵀ = Pᵀ∘(dPᵀ − δ)   (elementwise)
 //   dV += Pᵀ·dO_hf   (Pᵀ from TMEM)                      UMMA ts
 //   dK += dSᵀ·Q_hf   (dSᵀ from TMEM)                     UMMA ts
 // and per tile: dQ_t = dS·K (dS from shared memory, MN-major, double
@@ -20,13 +20,14 @@
 // dq_acc[t] += scale·dQ_t (fp32 vector reductions, red.global.add.v4.f32).
 //   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
 //                 written per head as key-major dS tiles, see pair_tiles.cu.
-// The pair bias enters through the tensor cores: c = 1/scale (a power of two,
-// so c·pair is exact in the fp32 accumulator) times the shifted identity of
-// fa_sm100.cuh as A, the pair tile [key][query] of the key-major per-head copy
-// pair_tiles() writes as the MN-major B operand.
+// The pair bias is read in the elementwise step from the key-major per-head
+// copy pair_tiles() writes: each half tile [128 keys][64 queries] is one TMA
+// box (128-byte swizzle), so a thread reads its key's 16 queries as two
+// conflict-free 16-byte vectors.  Half tiles rotate through a 3-slot ring, so
+// the next tile's first half is in flight while the current one is read.
 // Warp roles (512 threads):
 //   warp 0      TMA producer (K, V once; Q_t, dO_t into a 2-stage ring; the
-//               pair tile of (query tile, key tile, head), two 64-query boxes)
+//               pair half tiles of (query tile, key tile, head))
 //   warp 1      MMA issuer (one lane)
 //   warps 2-3   tile provider: lse (log2 units) and δ of the tile's queries
 //   warps 4-7   elementwise, query half 0 (one key per TMEM lane)
@@ -70,9 +71,9 @@ enum Bar {
     kTileFull = 13,   // +buffer: provider -> elementwise (64 arrivals)
     kTileEmpty = 15,  // +buffer: elementwise -> provider (256 arrivals)
     kFinal = 17,      // every MMA retired
-    kPairFull = 18,   // pair tile landed (TMA)
-    kPairEmpty = 19,  // its UMMAs retired
-    kNumBars = 20
+    kPairFull = 18,   // +slot: pair half tile landed (TMA)
+    kPairEmpty = 21,  // +slot: its warpgroup is done with it (128 arrivals)
+    kNumBars = 24
 };
 
 struct Lay {
@@ -83,10 +84,9 @@ struct Lay {
     static constexpr int kDO = kQ + 2 * kTile;      // 2 stages
     static constexpr int kDS = kDO + 2 * kTile;     // 2 buffers of [2 halves][128 keys][64 queries], MN-major SW128
     static constexpr int kDSBytes = 2 * kTile;
-    static constexpr int kPair = kDS + 2 * kDSBytes;   // [2 halves][BN keys][64 queries] SW128
-    static constexpr int kPairBytes = kBM * kBN * 2;
-    static constexpr int kEye = kPair + kPairBytes;     // shifted identity (1024-aligned)
-    static constexpr int kLse = kEye + kEyeBytes;       // [2][BM] float (log2 units)
+    static constexpr int kPair = kDS + 2 * kDSBytes;   // 3 slots of [BN keys][64 queries] SW128
+    static constexpr int kPairSlot = kBN * kHM * 2;
+    static constexpr int kLse = kPair + 3 * kPairSlot;  // [2][BM] float (log2 units)
     static constexpr int kDel = kLse + 2 * kBM * 4;     // [2][BM] float
     static constexpr int kBar = kDel + 2 * kBM * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
@@ -106,12 +106,29 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, ok);
 }
 
-// 16 columns of Pᵀ and dSᵀ from 16 columns of Sᵀ and dPᵀ; columns t outside
-// [lo, hi) are masked (probability 0).
-template <typename T, bool MASKED>
+// Two packed 16-bit values -> float (exact)
+template <typename T>
+__device__ __forceinline__ float lo16(uint32_t w);
+template <typename T>
+__device__ __forceinline__ float hi16(uint32_t w);
+template <>
+__device__ __forceinline__ float lo16<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w << 16); }
+template <>
+__device__ __forceinline__ float hi16<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+template <>
+__device__ __forceinline__ float lo16<__half>(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)w)); }
+template <>
+__device__ __forceinline__ float hi16<__half>(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+// 16 columns of Pᵀ and dSᵀ from 16 columns of Sᵀ and dPᵀ (and of the pair
+// bias, when PAIR); columns t outside [lo, hi) are masked (probability 0).
+template <typename T, bool PAIR, bool MASKED>
 __device__ __forceinline__ void elementwise16(const uint32_t (&sr)[16], const uint32_t (&dr)[16],
-                                              const float4 (&l4)[4], const float4 (&d4)[4], float sl2, int lo,
-                                              int hi, uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+                                              const uint32_t (&pw)[8], const float4 (&l4)[4],
+                                              const float4 (&d4)[4], float sl2, int lo, int hi, uint32_t (&pk)[8],
+                                              uint32_t (&dk)[8]) {
     const float* lse = reinterpret_cast<const float*>(l4);
     const float* del = reinterpret_cast<const float*>(d4);
 #pragma unroll
@@ -119,7 +136,9 @@ __device__ __forceinline__ void elementwise16(const uint32_t (&sr)[16], const ui
         float pv[2], dv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-            float pr = ex2(fmaf(__uint_as_float(sr[t + u]), sl2, -lse[t + u]));
+            float off = -lse[t + u];
+            if (PAIR) off = fmaf(u ? hi16<T>(pw[t >> 1]) : lo16<T>(pw[t >> 1]), kLog2e, off);
+            float pr = ex2(fmaf(__uint_as_float(sr[t + u]), sl2, off));
             if (MASKED) pr = (t + u >= lo && t + u < hi) ? pr : 0.f;
             pv[u] = pr;
             dv[u] = pr * (__uint_as_float(dr[t + u]) - del[t + u]);
@@ -171,13 +190,11 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_init(&bars[kDQFull], 1);
         mbar_init(&bars[kDQEmpty], 128);
         mbar_init(&bars[kFinal], 1);
-        mbar_init(&bars[kPairFull], 1);
-        mbar_init(&bars[kPairEmpty], 1);
+        for (int s = 0; s < 3; ++s) {
+            mbar_init(&bars[kPairFull + s], 1);
+            mbar_init(&bars[kPairEmpty + s], 128);
+        }
         fence_mbar_init();
-    }
-    if (PAIR) {
-        build_eye<T>(smem + Lay::kEye, 1.f / p.scale, threadIdx.x, kThreads);
-        fence_proxy_async_smem();   // identity writes -> UMMA reads
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -202,7 +219,21 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             tma_load_3d(smem + Lay::kK, &tm_k, &bars[kKVFull], 0, (int)k0, bh_k);
             tma_load_3d(smem + Lay::kV, &tm_v, &bars[kKVFull], 0, (int)k0, bh_k);
             int issued = 0, pair_issued = 0;
-            for (int t = 0; t < tiles; ++t) {
+            // pair half tile n = 2t + hf goes to slot n % 3 once half tile n - 3 is consumed
+            auto load_pair = [&](int n) -> bool {
+                const int slot = n % 3;
+                if (n >= 3 && !wait(&bars[kPairEmpty + slot], ((n / 3) - 1) & 1, ab, 1)) return false;
+                const int t = n >> 1, hf = n & 1;
+                const int h = kvh * p.n_rep + t / nq;
+                const int q0 = (qt0 + t % nq) * kBM;
+                mbar_expect_tx(&bars[kPairFull + slot], Lay::kPairSlot);
+                tma_load_3d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot],
+                            q0 + hf * kHM, (int)k0, b * QH + h);
+                pair_issued = n + 1;
+                return true;
+            };
+            bool run = true;
+            for (int t = 0; run && t < tiles; ++t) {
                 const int s = t & 1;
                 if (t >= 2 && !wait(&bars[kQEmpty + s], ((t >> 1) - 1) & 1, ab, 0)) break;
                 const int h = kvh * p.n_rep + t / nq;
@@ -211,36 +242,26 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tma_load_3d(smem + Lay::kQ + s * Lay::kTile, &tm_q, &bars[kQFull + s], 0, q0, b * QH + h);
                 tma_load_3d(smem + Lay::kDO + s * Lay::kTile, &tm_do, &bars[kQFull + s], 0, q0, b * QH + h);
                 issued = t + 1;
-                if (PAIR) {
-                    if (t >= 1 && !wait(&bars[kPairEmpty], (t - 1) & 1, ab, 1)) break;
-                    mbar_expect_tx(&bars[kPairFull], Lay::kPairBytes);
-#pragma unroll
-                    for (int half = 0; half < 2; ++half)
-                        tma_load_3d(smem + Lay::kPair + half * kBN * 128, &tm_pair, &bars[kPairFull],
-                                    q0 + half * kHM, (int)k0, b * QH + h);
-                    pair_issued = t + 1;
-                }
+                if (PAIR) run = load_pair(2 * t) && load_pair(2 * t + 1);
             }
             // copies in flight land before the CTA leaves (bounded waits)
             wait(&bars[kKVFull], 0, ab, 2);
             for (int t = issued - 2 < 0 ? 0 : issued - 2; t < issued; ++t)
                 wait(&bars[kQFull + (t & 1)], (t >> 1) & 1, ab, 2);
-            if (PAIR && pair_issued > 0) wait(&bars[kPairFull], (pair_issued - 1) & 1, ab, 2);
+            for (int n = pair_issued - 3 < 0 ? 0 : pair_issued - 3; n < pair_issued; ++n)
+                wait(&bars[kPairFull + n % 3], (n / 3) & 1, ab, 2);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         constexpr uint32_t id_s = idesc_f16<kBF16>(128, kHM, false, false);   // Sᵀ, dPᵀ of a half
-        constexpr uint32_t id_p = idesc_f16<kBF16>(128, kHM, false, true);    // Sᵀ += c·I·pairᵀ
         constexpr uint32_t id_kv = idesc_f16<kBF16>(128, kE, false, true);    // dV, dK (A in TMEM)
         constexpr uint32_t id_q = idesc_f16<kBF16>(128, kE, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
-        const uint32_t sEye = smem_u32(smem + Lay::kEye), sP = smem_u32(smem + Lay::kPair);
-        // Sᵀ/dPᵀ (+ pair) of half hf of tile t into the half's TMEM buffers
+        // Sᵀ/dPᵀ of half hf of tile t into the half's TMEM buffers
         auto issue_s = [&](int t, int hf) -> bool {
             const int s = t & 1;
             if (hf == 0) {
                 if (!wait_warp(&bars[kQFull + s], (t >> 1) & 1, ab, 4)) return false;
-                if (PAIR && !wait_warp(&bars[kPairFull], t & 1, ab, 5)) return false;
                 tc_fence_after();
             }
             if (lane == 0) {
@@ -251,14 +272,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 for (int kk = 0; kk < kE / 16; ++kk) {
                     umma_ss(dS, desc_k_sw128(sK + kk * 32), desc_k_sw128(sQ + kk * 32), id_s, kk > 0 ? 1u : 0u);
                     umma_ss(dDP, desc_k_sw128(sV + kk * 32), desc_k_sw128(sDO + kk * 32), id_s, kk > 0 ? 1u : 0u);
-                }
-                if (PAIR) {
-                    // B = pair half [key][64 queries]: MN-major over queries, K = keys
-#pragma unroll
-                    for (int kk = 0; kk < kBN / 16; ++kk)
-                        umma_ss(dS, desc_k_sw128(eye_step(sEye, kk)),
-                                desc_mn_sw128(sP + hf * kBN * 128 + kk * 16 * 128, 0), id_p, 1u);
-                    if (hf == 1) umma_commit(&bars[kPairEmpty]);
                 }
                 umma_commit(&bars[kSFull + hf]);
             }
@@ -340,6 +353,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             if (!wait_warp(&bars[kTileFull + buf], (t >> 1) & 1, ab, 10)) break;
             if (!wait_warp(&bars[kSFull + hf], t & 1, ab, 11)) break;
             if (t >= 2 && !wait_warp(&bars[kDSEmpty + buf], ((t >> 1) - 1) & 1, ab, 12)) break;
+            const int pn = 2 * t + hf, pslot = pn % 3;
+            if (PAIR && !wait_warp(&bars[kPairFull + pslot], (pn / 3) & 1, ab, 5)) break;
             tc_fence_after();
             // valid query columns of this key within the half: [cmin, cmax)
             const int64_t nvq = QL - qh0;
@@ -351,6 +366,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             uint8_t* sDS = smem + Lay::kDS + buf * Lay::kDSBytes + hf * (kBN * 128) + jr * 128;
             const float* lse_h = sLse + buf * kBM + hf * kHM;
             const float* del_h = sDel + buf * kBM + hf * kHM;
+            const uint8_t* prow = smem + Lay::kPair + pslot * Lay::kPairSlot + jr * 128;
 #pragma unroll 1
             for (int cc = 0; cc < kHM / 16; ++cc) {
                 const int col = cc * 16;
@@ -363,13 +379,21 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     l4[v] = reinterpret_cast<const float4*>(lse_h + col)[v];
                     d4[v] = reinterpret_cast<const float4*>(del_h + col)[v];
                 }
+                uint32_t pw[8];
+                if (PAIR) {
+#pragma unroll
+                    for (int v = 0; v < 2; ++v) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(prow + (((cc * 2 + v) ^ (jr & 7)) << 4));
+                        pw[4 * v] = u.x; pw[4 * v + 1] = u.y; pw[4 * v + 2] = u.z; pw[4 * v + 3] = u.w;
+                    }
+                }
                 tmem_ld_wait();
                 uint32_t pk[8], dk[8];
                 const int lo = cmin - col, hi = cmax - col;
                 if (lo <= 0 && hi >= 16)
-                    elementwise16<T, false>(sr, dr, l4, d4, sl2, 0, 16, pk, dk);
+                    elementwise16<T, PAIR, false>(sr, dr, pw, l4, d4, sl2, 0, 16, pk, dk);
                 else
-                    elementwise16<T, true>(sr, dr, l4, d4, sl2, lo, hi, pk, dk);
+                    elementwise16<T, PAIR, true>(sr, dr, pw, l4, d4, sl2, lo, hi, pk, dk);
                 tmem_st8(tSh + cc * 8, pk);
                 tmem_st8(tDPh + cc * 8, dk);
                 // dS (16-bit) into shared memory for the dQ MMA: row jr, queries
@@ -388,6 +412,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 }
             }
             mbar_arrive(&bars[kTileEmpty + buf]);
+            if (PAIR) mbar_arrive(&bars[kPairEmpty + pslot]);
             tmem_st_wait();
             fence_proxy_async_smem();   // dS smem writes -> tensor-core (async proxy) reads
             tc_fence_before();
