@@ -19,7 +19,9 @@
 // buffered so the next tile's dS can be written meanwhile), then
 // dq_acc[t] += scale·dQ_t (fp32 vector reductions, red.global.add.v4.f32).
 //   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
-//                 written per head as key-major dS tiles, see pair_tiles.cu.
+//                 written per head as key-major dS tiles, see pair_tiles.cu:
+//                 the MMA warp stores each finished dS half from shared memory
+//                 with one TMA store (the buffer's layout is the tile's box).
 // The pair bias is read in the elementwise step from the key-major per-head
 // copy pair_tiles() writes: each half tile [128 keys][64 queries] is one TMA
 // box (128-byte swizzle), so a thread reads its key's 16 queries as two
@@ -152,8 +154,8 @@ template <typename T, bool CAUSAL, bool PAIR, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const __grid_constant__ CUtensorMap tm_pair, const Params p, uint16_t* __restrict__ ds_tiles,
-                    int64_t qlp, int64_t klp) {
+                    const __grid_constant__ CUtensorMap tm_pair, const __grid_constant__ CUtensorMap tm_ds,
+                    const Params p) {
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -285,6 +287,17 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             for (int hf = 0; hf < 2; ++hf) {
                 if (!wait_warp(&bars[kPFull + hf], t & 1, ab, 6)) { ok = false; break; }
                 tc_fence_after();
+                if (PAIR && lane == 0) {
+                    // dS half -> per-head dS tiles; before the half's next score
+                    // tile lets its warpgroup refill the other dS buffer, the
+                    // store issued two halves ago must have read its source.
+                    const int h = kvh * p.n_rep + t / nq;
+                    const int q0 = (qt0 + t % nq) * kBM;
+                    tma_store_3d(&tm_ds, smem + Lay::kDS + s * Lay::kDSBytes + hf * kBN * 128, q0 + hf * kHM, (int)k0,
+                                 b * QH + h);
+                    bulk_commit();
+                    bulk_wait_read<2>();
+                }
                 if (lane == 0) {
                     const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile) + hf * kHM * 128;
                     const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile) + hf * kHM * 128;
@@ -316,6 +329,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             }
             __syncwarp();
         }
+        // dS stores land before the CTA exits
+        if (PAIR && lane == 0) bulk_wait<0>();
         // every MMA this warp issued retires before TMEM is read out / freed
         if (lane == 0) umma_commit(&bars[kFinal]);
         __syncwarp();
@@ -348,7 +363,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const float sl2 = p.scale * kLog2e;
         for (int t = 0; t < tiles; ++t) {
             const int buf = t & 1;
-            const int h = kvh * p.n_rep + t / nq;
             const int64_t qh0 = (int64_t)(qt0 + t % nq) * kBM + hf * kHM;   // first query of the half
             if (!wait_warp(&bars[kTileFull + buf], (t >> 1) & 1, ab, 10)) break;
             if (!wait_warp(&bars[kSFull + hf], t & 1, ab, 11)) break;
@@ -361,8 +375,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const int cmax = key_ok ? (int)(nvq < kHM ? (nvq > 0 ? nvq : 0) : kHM) : 0;
             const int64_t cm = CAUSAL ? j - qh0 : 0;
             const int cmin = (int)(cm < 0 ? 0 : (cm > kHM ? kHM : cm));
-            // dS row of this key in the per-head tiles: [b][h][key][query]
-            uint16_t* dst_row = PAIR ? ds_tiles + (((int64_t)b * QH + h) * klp + j) * qlp + qh0 : nullptr;
             uint8_t* sDS = smem + Lay::kDS + buf * Lay::kDSBytes + hf * (kBN * 128) + jr * 128;
             const float* lse_h = sLse + buf * kBM + hf * kHM;
             const float* del_h = sDel + buf * kBM + hf * kHM;
@@ -403,12 +415,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     const int chunk = cc * 2 + v;
                     *reinterpret_cast<uint4*>(sDS + ((chunk ^ (jr & 7)) << 4)) =
                         make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]);
-                }
-                if (PAIR) {
-#pragma unroll
-                    for (int v = 0; v < 2; ++v)
-                        __stcs(reinterpret_cast<uint4*>(dst_row + col + v * 8),
-                               make_uint4(dk[4 * v], dk[4 * v + 1], dk[4 * v + 2], dk[4 * v + 3]));
                 }
             }
             mbar_arrive(&bars[kTileEmpty + buf]);
@@ -481,19 +487,21 @@ template <typename T, bool CAUSAL, bool PAIR, bool MASK>
 int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t s) {
     constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     const int64_t qlp = (p.QL + 127) / 128 * 128, klp = (p.KL + 127) / 128 * 128;
-    CUtensorMap tq, tk, tv, tdo, tp;
+    CUtensorMap tq, tk, tv, tdo, tp, tds;
     memset(&tp, 0, sizeof(tp));
+    memset(&tds, 0, sizeof(tds));
     if (!make_map(&tq, p.q, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
-        (PAIR && !make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16)))
+        (PAIR && (!make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16) ||
+                  !make_map(&tds, ds_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16))))
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_bwd_sm100_kernel<T, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cannot set shared memory size");
     dim3 grid((unsigned)((p.KL + kBN - 1) / kBN), p.KH, p.B);
-    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tdo, tp, p, static_cast<uint16_t*>(ds_tiles), qlp, klp);
+    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tdo, tp, tds, p);
     return check_launch("flash_attention_bwd (sm100)");
 }
 
