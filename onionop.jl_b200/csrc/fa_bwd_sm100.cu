@@ -17,7 +17,8 @@
 //   dK += dSᵀ·Q_hf   (dSᵀ from TMEM)                     UMMA ts
 // and per tile: dQ_t = dS·K (dS from shared memory, MN-major, double
 // buffered so the next tile's dS can be written meanwhile), then
-// dq_acc[t] += scale·dQ_t (fp32 vector reductions, red.global.add.v4.f32).
+// dq_acc[t] += scale·dQ_t: the dQ warps stage the fp32 rows in the tile's
+// consumed dS buffer (128-byte swizzle) and add them with TMA reduce-adds.
 //   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
 //                 written per head as key-major dS tiles, see pair_tiles.cu:
 //                 the MMA warp stores each finished dS half from shared memory
@@ -34,7 +35,7 @@
 //   warps 2-3   tile provider: lse (log2 units) and δ of the tile's queries
 //   warps 4-7   elementwise, query half 0 (one key per TMEM lane)
 //   warps 8-11  elementwise, query half 1
-//   warps 12-15 dQ: TMEM dQ rows -> fp32 reductions into the accumulator
+//   warps 12-15 dQ: TMEM dQ rows -> staged fp32 boxes -> TMA reduce-add
 // TMEM columns: Sᵀ half 0 [0,64), half 1 [64,128), dPᵀ half 0 [128,192),
 // half 1 [192,256), dV [256,320), dK [320,384), dQ [384,448).  The 16-bit
 // Pᵀ / dSᵀ of a half overwrite the first 32 columns of its own score buffers.
@@ -67,7 +68,7 @@ enum Bar {
     kQEmpty = 3,      // +stage: dV/dK MMAs of the tile retired
     kSFull = 5,       // +half: Sᵀ, dPᵀ of the half in TMEM
     kPFull = 7,       // +half: elementwise done with the half (128 arrivals)
-    kDSEmpty = 9,     // +buffer: dQ MMA done reading the dS buffer
+    kDSEmpty = 9,     // +buffer: dQ staging done with the dS buffer (4 arrivals)
     kDQFull = 11,     // dQ_t in TMEM
     kDQEmpty = 12,    // dQ warps done with TMEM dQ (128 arrivals)
     kTileFull = 13,   // +buffer: provider -> elementwise (64 arrivals)
@@ -97,10 +98,6 @@ struct Lay {
 };
 static_assert(Lay::kAlloc <= 227 * 1024, "shared memory");
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
-}
 // Warp-uniform bounded wait: true only if every lane saw the phase complete
 // (guards warp-wide tcgen05.ld/st, which must not run divergent).
 __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* ab, int site) {
@@ -155,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_pair, const __grid_constant__ CUtensorMap tm_ds,
-                    const Params p) {
+                    const __grid_constant__ CUtensorMap tm_dq, const Params p) {
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -185,7 +182,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             mbar_init(&bars[kQEmpty + s], 1);
             mbar_init(&bars[kSFull + s], 1);
             mbar_init(&bars[kPFull + s], 128);
-            mbar_init(&bars[kDSEmpty + s], 1);
+            mbar_init(&bars[kDSEmpty + s], 4);
             mbar_init(&bars[kTileFull + s], 64);
             mbar_init(&bars[kTileEmpty + s], 256);
         }
@@ -324,8 +321,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 for (int kk = 0; kk < kBN / 16; ++kk)
                     umma_ss(tDQ, desc_mn_sw128(sDS + kk * 16 * 128, kBN * 128), desc_mn_sw128(sK + kk * 16 * 128, 0),
                             id_q, kk > 0 ? 1u : 0u);
+                // the dQ warps reuse this dS buffer as staging once dQ_t is
+                // done: the dS stores must have read it by then
+                if (PAIR) bulk_wait_read<0>();
                 umma_commit(&bars[kDQFull]);
-                umma_commit(&bars[kDSEmpty + s]);
             }
             __syncwarp();
         }
@@ -450,30 +449,47 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         }
     } else {
         // ------------------------------------------------------ dQ reductions
-        const int r = threadIdx.x - 384;                      // query row = TMEM lane
-        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        // warp w: query rows 32w..32w+31 of the tile (TMEM lanes), staged as
+        // two [32 rows][32 floats] boxes, 128-byte swizzle, in the tile's dS
+        // buffer, then one TMA reduce-add per box into dq_acc (rows past QL
+        // are clipped by the tensor map)
+        const int w = warp & 3;
+        const uint32_t lane_off = (uint32_t)(w * 32) << 16;
         for (int t = 0; t < tiles; ++t) {
             const int h = kvh * p.n_rep + t / nq;
-            const int64_t i = (int64_t)(qt0 + t % nq) * kBM + r;
+            const int q0 = (qt0 + t % nq) * kBM;
             if (!wait_warp(&bars[kDQFull], t & 1, ab, 14)) break;
             tc_fence_after();
-            float* dq = p.dq_acc + (((int64_t)b * QH + h) * QL + i) * kE;
+            uint32_t raw[4][16];
 #pragma unroll
-            for (int c = 0; c < kE / 16; ++c) {
-                uint32_t raw[16];
-                tmem_ld16(tDQ + lane_off + c * 16, raw);
-                tmem_ld_wait();
-                if (i < QL) {
+            for (int c = 0; c < 4; ++c) tmem_ld16(tDQ + lane_off + c * 16, raw[c]);
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(&bars[kDQEmpty]);   // TMEM dQ may be overwritten
+            uint8_t* stg = smem + Lay::kDS + (t & 1) * Lay::kDSBytes + w * 8192;
 #pragma unroll
-                    for (int v = 0; v < 4; ++v)
-                        red_add_v4(dq + c * 16 + 4 * v, __uint_as_float(raw[4 * v]) * p.scale,
-                                   __uint_as_float(raw[4 * v + 1]) * p.scale, __uint_as_float(raw[4 * v + 2]) * p.scale,
-                                   __uint_as_float(raw[4 * v + 3]) * p.scale);
+            for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int chunk = (c & 1) * 4 + v;
+                    *reinterpret_cast<float4*>(stg + (c >> 1) * 4096 + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+                        make_float4(__uint_as_float(raw[c][4 * v]) * p.scale, __uint_as_float(raw[c][4 * v + 1]) * p.scale,
+                                    __uint_as_float(raw[c][4 * v + 2]) * p.scale,
+                                    __uint_as_float(raw[c][4 * v + 3]) * p.scale);
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&bars[kDQEmpty]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_reduce_add_3d(&tm_dq, stg, 0, q0 + 32 * w, b * QH + h);
+                tma_reduce_add_3d(&tm_dq, stg + 4096, 32, q0 + 32 * w, b * QH + h);
+                bulk_commit();
+                bulk_wait_read<0>();
+                mbar_arrive(&bars[kDSEmpty + (t & 1)]);
+            }
+            __syncwarp();
         }
+        if (lane == 0) bulk_wait<0>();   // reductions land before the CTA exits
     }
     tc_fence_before();
     __syncthreads();
@@ -483,17 +499,33 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
 }
 
+// 3-D map over the fp32 dQ accumulator [B·QH][QL][64], box (32, 32, 1),
+// 128-byte swizzle (the dQ warps' staging layout).
+bool make_dq_map(CUtensorMap* m, float* base, int64_t QL, int64_t bh) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)kE, (cuuint64_t)QL, (cuuint64_t)bh};
+    cuuint64_t strides[2] = {(cuuint64_t)kE * 4, (cuuint64_t)QL * kE * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 template <typename T, bool CAUSAL, bool PAIR, bool MASK>
 int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t s) {
     constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     const int64_t qlp = (p.QL + 127) / 128 * 128, klp = (p.KL + 127) / 128 * 128;
-    CUtensorMap tq, tk, tv, tdo, tp, tds;
+    CUtensorMap tq, tk, tv, tdo, tp, tds, tdq;
     memset(&tp, 0, sizeof(tp));
     memset(&tds, 0, sizeof(tds));
     if (!make_map(&tq, p.q, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
+        !make_dq_map(&tdq, p.dq_acc, p.QL, (int64_t)p.B * p.QH) ||
         (PAIR && (!make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16) ||
                   !make_map(&tds, ds_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16))))
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cuTensorMapEncodeTiled failed");
@@ -501,7 +533,7 @@ int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cannot set shared memory size");
     dim3 grid((unsigned)((p.KL + kBN - 1) / kBN), p.KH, p.B);
-    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tdo, tp, tds, p);
+    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tdo, tp, tds, tdq, p);
     return check_launch("flash_attention_bwd (sm100)");
 }
 
