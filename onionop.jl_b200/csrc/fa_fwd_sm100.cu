@@ -296,25 +296,40 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             if (!wait_warp(&bars[kSFull + buf], (j >> 1) & 1, ab, 13)) { ok = false; break; }
             tc_fence_after();
             const uint32_t tS = (buf ? tS1 : tS0) + lane_off;
+            // all four 32-column loads in flight at once
+            uint32_t raw[kBN];
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c)
+                tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(raw + c * 32));
+            // words past the last key are never read: k0 + c·32 < n_words·32 here
+            uint32_t vb[kBN / 32];
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c) vb[c] = (k0 + c * 32 < KL) ? bits[(k0 >> 5) + c] : 0u;
+            // keys k0 + t visible to this row: t <= kr (causal)
+            const int64_t kr64 = i - k0;
+            const int kr = (int)(kr64 < 0 ? -1 : (kr64 > kBN ? kBN : kr64));
+            const bool full = (!CAUSAL || kr >= kBN - 1) && (vb[0] & vb[1] & vb[2] & vb[3]) == 0xffffffffu;
+            tmem_ld_wait();
             float x[kBN];
+            if (full) {
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t raw[32];
-                tmem_ld32(tS + c * 32, raw);
-                tmem_ld_wait();
-                // words past the last key are never read: k0 + c·32 < n_words·32 here
-                const uint32_t vbits = (k0 + c * 32 < KL) ? bits[(k0 >> 5) + c] : 0u;
+                for (int t = 0; t < kBN; ++t) x[t] = __uint_as_float(raw[t]) * sl2;
+            } else {
 #pragma unroll
-                for (int t = 0; t < 32; ++t) {
-                    const float v = __uint_as_float(raw[t]) * sl2;
-                    bool valid = (vbits >> t) & 1u;
-                    if (CAUSAL) valid = valid && (k0 + c * 32 + t <= i);
-                    x[c * 32 + t] = valid ? v : -INFINITY;
+                for (int t = 0; t < kBN; ++t) {
+                    bool valid = (vb[t >> 5] >> (t & 31)) & 1u;
+                    if (CAUSAL) valid = valid && (t <= kr);
+                    x[t] = valid ? __uint_as_float(raw[t]) * sl2 : -INFINITY;
                 }
             }
-            float mx = x[0];
+            // row max and sum over 8 independent partials (short dependency chains)
+            float mp[8];
 #pragma unroll
-            for (int t = 1; t < kBN; ++t) mx = fmaxf(mx, x[t]);
+            for (int u = 0; u < 8; ++u) mp[u] = x[u];
+#pragma unroll
+            for (int t = 8; t < kBN; ++t) mp[t & 7] = fmaxf(mp[t & 7], x[t]);
+            const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                                   fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
             float alpha = 1.f;
             const float m_new = fmaxf(m, mx);
             const bool resc = m_new > m + 8.f;
@@ -323,7 +338,9 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 m = m_new;
             }
             const float m_use = (m == -INFINITY) ? 0.f : m;
-            float ls = 0.f;
+            float sp[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sp[u] = 0.f;
 #pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t pk[16];
@@ -331,11 +348,13 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 for (int t = 0; t < 16; ++t) {
                     const float p0 = ex2(x[c * 32 + 2 * t] - m_use);
                     const float p1 = ex2(x[c * 32 + 2 * t + 1] - m_use);
-                    ls += p0 + p1;
+                    sp[(2 * t) & 7] += p0;
+                    sp[(2 * t + 1) & 7] += p1;
                     pk[t] = pack16<T>(p0, p1);
                 }
                 tmem_st16(tS + c * 16, pk);
             }
+            const float ls = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
             l = l * alpha + ls;
             // O rescale: the decision is per row, the TMEM access per warp, so
             // the whole warp takes the branch when any of its rows needs it
