@@ -226,8 +226,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 const int h = kvh * p.n_rep + t / nq;
                 const int q0 = (qt0 + t % nq) * kBM;
                 mbar_expect_tx(&bars[kPairFull + slot], Lay::kPairSlot);
-                tma_load_3d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot],
-                            q0 + hf * kHM, (int)k0, b * QH + h);
+                tma_load_4d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot], hf * kHM,
+                            (int)k0, q0 / kBM, b * QH + h);
                 pair_issued = n + 1;
                 return true;
             };
@@ -290,8 +290,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     // store issued two halves ago must have read its source.
                     const int h = kvh * p.n_rep + t / nq;
                     const int q0 = (qt0 + t % nq) * kBM;
-                    tma_store_3d(&tm_ds, smem + Lay::kDS + s * Lay::kDSBytes + hf * kBN * 128, q0 + hf * kHM, (int)k0,
-                                 b * QH + h);
+                    tma_store_4d(&tm_ds, smem + Lay::kDS + s * Lay::kDSBytes + hf * kBN * 128, hf * kHM, (int)k0,
+                                 q0 / kBM, b * QH + h);
                     bulk_commit();
                     bulk_wait_read<2>();
                 }
@@ -526,8 +526,8 @@ int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t
         !make_map(&tv, p.v, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_dq_map(&tdq, p.dq_acc, p.QL, (int64_t)p.B * p.QH) ||
-        (PAIR && (!make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16) ||
-                  !make_map(&tds, ds_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16))))
+        (PAIR && (!make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16) ||
+                  !make_tiles_map(&tds, ds_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16))))
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_bwd_sm100_kernel<T, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)

@@ -8,7 +8,7 @@
 //   warp 0     TMA producer: Q once, then K_j / V_j into a 2-stage ring and,
 //              with a pair bias, the pair tile of (q-tile, k-tile j, head)
 //              from the key-major per-head copy pair_tiles() writes
-//              ([B][H][KL][QL], two 64-query boxes: [key][query] per half);
+//              ([B][H][QL/128][KL][128], two 64-query boxes: [key][query]);
 //   warp 1     MMA issuer: S_j = Q·K_jᵀ into one of two TMEM score buffers,
 //              plus, with a pair bias, S_j += c·I·pair_jᵀ (c = 1/scale; the
 //              pair tile is the K-major B operand of a 128x128x128 UMMA
@@ -207,8 +207,8 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     mbar_expect_tx(&bars[kPairFull + (j & 1)], L::kPairBytes);
 #pragma unroll
                     for (int half = 0; half < 2; ++half)
-                        tma_load_3d(smem + L::kPair + (j & 1) * L::kPairBytes + half * kBN * 128, &tm_pair,
-                                    &bars[kPairFull + (j & 1)], (int)q0 + half * 64, k0, bh_q);
+                        tma_load_4d(smem + L::kPair + (j & 1) * L::kPairBytes + half * kBN * 128, &tm_pair,
+                                    &bars[kPairFull + (j & 1)], half * 64, k0, qt, bh_q);
                 }
             }
             // Copies still in flight must land before the CTA can exit (they
@@ -427,7 +427,7 @@ int launch(const Params& p, const void* pair_tiles, cudaStream_t s) {
     if (!make_map(&tq, p.q, E, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
-        (PAIR && !make_map(&tp, pair_tiles, (int)qlp, klp, (int64_t)p.B * p.QH, kBN, bf16)))
+        (PAIR && !make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16)))
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_fwd_sm100_kernel<T, E, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)

@@ -93,6 +93,22 @@ bool make_map(CUtensorMap* m, const void* base, int E, int64_t rows, int64_t bh,
     return r == CUDA_SUCCESS;
 }
 
+// 4-D map over the per-head pair / dS tiles [B·H][QLp/128][KLp][128]
+// (pair_tiles.cu), box (64, 128, 1, 1): one 64-query half of a (128-query,
+// 128-key) tile, 128-byte swizzle.
+bool make_tiles_map(CUtensorMap* m, const void* base, int64_t qlp, int64_t klp, int64_t bh, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {128, (cuuint64_t)klp, (cuuint64_t)(qlp / 128), (cuuint64_t)bh};
+    cuuint64_t strides[3] = {256, (cuuint64_t)klp * 256, (cuuint64_t)(qlp / 128) * klp * 256};
+    cuuint32_t box[4] = {64, 128, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace
 }  // namespace fa
 }  // namespace nnop

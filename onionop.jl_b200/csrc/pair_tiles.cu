@@ -5,8 +5,9 @@
 // buffer [B][KL][QL][H]: one head's element is 2 bytes of every 32-byte sector
 // (H = 16), so a CTA that owns one head cannot read it efficiently.  The
 // attention kernels instead read, per head, the key-major copy
-//   tiles[b][h][key][query]          (QL, KL padded to multiples of 128)
-// whose (128-query, 128-key) tile is two 64-query TMA boxes.  The forward uses
+//   tiles[b][h][query/128][key][query%128]   (QL, KL padded to multiples of 128)
+// in which a (128-query, 128-key) tile is one contiguous 32 KB block, two
+// 64-query TMA boxes.  The forward uses
 // it as the K-major, the backward as the MN-major B operand of an identity
 // UMMA that adds the bias to the scores (fa_fwd_sm100.cu, fa_bwd_sm100.cu);
 // the backward writes its dS tiles in the same layout and dpair_from_tiles
@@ -83,7 +84,7 @@ __device__ __forceinline__ bool visited(int c, int64_t g, int b, const int* kv_l
     return true;
 }
 
-// tiles[b][h][g*8+kk][i0+i] = pair[b][g*8+kk][i0+i][h];
+// tiles[b][h][c][g*8+kk][i] = pair[b][g*8+kk][c*128+i][h];
 // block = (query chunk c, key group g, b)
 template <typename T>
 __global__ void __launch_bounds__(kTB, 2) pair_tiles_kernel(const T* __restrict__ pair, T* __restrict__ out,
@@ -106,12 +107,12 @@ __global__ void __launch_bounds__(kTB, 2) pair_tiles_kernel(const T* __restrict_
 #pragma unroll
         for (int e = 0; e < 4; ++e)
             w[e] = finite_lo<T>(col[(2 * e) * H]) | (finite_lo<T>(col[(2 * e + 1) * H]) << 16);
-        T* dst = out + (((int64_t)b * H + h) * klp + g * kKeys + kk) * qlp + i0 + v * 8;
+        T* dst = out + ((((int64_t)b * H + h) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
         __stcs(reinterpret_cast<uint4*>(dst), make_uint4(w[0], w[1], w[2], w[3]));
     }
 }
 
-// dpair[b][g*8+kk][i][h] = tiles[b][h][g*8+kk][i] on visited blocks, 0 elsewhere.
+// dpair[b][g*8+kk][c*128+i][h] = tiles[b][h][c][g*8+kk][i] on visited blocks, 0 elsewhere.
 template <typename T>
 __global__ void __launch_bounds__(kTB) dpair_from_tiles_kernel(const T* __restrict__ tiles, T* __restrict__ dpair,
                                                                const int* __restrict__ kv_len, int64_t QL,
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(kTB) dpair_from_tiles_kernel(const T* __restri
                 if (x < total) {
                     const int h = x % H, v = (x / H) % (kTile / 8), kk = x / (H * (kTile / 8));
                     u[it] = __ldcs(reinterpret_cast<const uint4*>(
-                        tiles + (((int64_t)b * H + h) * klp + g * kKeys + kk) * qlp + i0 + v * 8));
+                        tiles + ((((int64_t)b * H + h) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8));
                 }
             }
 #pragma unroll
@@ -256,7 +257,7 @@ __global__ void __launch_bounds__(kTB, 3) pair_tiles_fast_kernel(const T* __rest
             lo[j] = finite2<T>(__byte_perm(w[2 * j], w[2 * j + 1], 0x5410));
             hi[j] = finite2<T>(__byte_perm(w[2 * j], w[2 * j + 1], 0x7632));
         }
-        T* dst = out + (((int64_t)b * H + 2 * hp) * klp + g * kKeys + kk) * qlp + i0 + v * 8;
+        T* dst = out + ((((int64_t)b * H + 2 * hp) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
         __stcs(reinterpret_cast<uint4*>(dst), make_uint4(lo[0], lo[1], lo[2], lo[3]));
         __stcs(reinterpret_cast<uint4*>(dst + klp * qlp), make_uint4(hi[0], hi[1], hi[2], hi[3]));
     }
@@ -289,7 +290,8 @@ __global__ void __launch_bounds__(kTB, 3) dpair_from_tiles_fast_kernel(const T* 
                 const int x = x0 + t * kTB + threadIdx.x;
                 if (x < kPieces) {
                     const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
-                    const T* p0 = tiles + (((int64_t)b * H + 2 * hp) * klp + g * kKeys + kk) * qlp + i0 + v * 8;
+                    const T* p0 =
+                        tiles + ((((int64_t)b * H + 2 * hp) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
                     a[t] = __ldcs(reinterpret_cast<const uint4*>(p0));
                     bq[t] = __ldcs(reinterpret_cast<const uint4*>(p0 + klp * qlp));
                 }
