@@ -38,15 +38,9 @@ def cfg_flops(B, H, L, E, causal):
     return fwd, 2.5 * fwd
 
 
-def cfg_bytes(B, H, L, E, causal, esz=2):
-    """Algorithmic HBM bytes of one fwd+bwd (dense tensors once each; pair read
-    over the causal half in fwd and bwd; dpair written in full)."""
-    c = 0.5 if causal else 1.0
-    pair = B * H * L * L * esz
-    qkvo = B * H * L * E * esz
-    fwd = c * pair + 3 * qkvo + qkvo                # read q,k,v,pair; write o
-    bwd = c * pair + pair + 5 * qkvo + 3 * qkvo     # read q,k,v,o,dO,pair; write dq,dk,dv,dpair
-    return fwd, bwd
+# DRAM bytes (read + write) of one fa_bwd_sm100_kernel launch of config 2 at
+# B = 1, from ncu (profiles/fa_bwd_sm100_config2_b1.md).
+TRAFFIC_BWD_B1 = 594.0e6
 
 
 def peaks():
@@ -55,6 +49,35 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+# --------------------------------------------------------------- ranks
+def dist_env():
+    """(rank, local_rank, world) from the torchrun environment (1 process = 1 GPU)."""
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def rank_seed(rank: int) -> int:
+    """Seed of a rank's synthetic batch shard: every rank processes its own
+    B = 8 slice (weak scaling; no data-path collective)."""
+    return 1000 + rank
+
+
+def max_over_ranks(values, device, world: int):
+    """Element-wise maximum of per-rank timings (one all-reduce after the timed
+    region; every rank takes this same collective step)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def job_tflops(flops_per_rank: float, world: int, max_ms: float) -> float:
+    """Whole-job throughput: the work of all ranks over the slowest rank's time."""
+    return flops_per_rank * world / (max_ms / 1e3) / 1e12
 
 
 # --------------------------------------------------------------- clocks
@@ -186,17 +209,14 @@ def host_threads():
 
 
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    rank, _, _ = dist_env()
+    if rank != 0:   # under torchrun the other ranks exit without work
         return
     K, W = args.steps, args.warmup
-    import numpy as np  # noqa: F401
     # each step: one (batch, head) slice of the workload, fwd + bwd
-    per_step = max(1, 1)
     times = []
     for i in range(W + K):
-        t0 = time.perf_counter()
-        tf, n, dt = cpu_attention_sample(seconds=0.0, max_heads=per_step)
+        tf, n, dt = cpu_attention_sample(seconds=0.0, max_heads=1)
         if i >= W:
             times.append(dt)
     fwd, bwd = cfg_flops(1, 1, CFG["L"], CFG["E"], True)
@@ -208,8 +228,9 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 bf16 causal pair-bias FA fwd+bwd, sampled on CPU", "E": 64, "L": 4096,
-                   "H": 16, "B": 8, "causal": True},
+        "config": {"workload": "config2: flash_attention fwd+bwd bf16 causal + pair bias", "E": 64, "L": 4096,
+                   "H": 16, "B_per_gpu": 8, "global_batch": 8 * args.gpus, "causal": True,
+                   "parallelism": "reference CPU implementation (oracle port), rank 0 only"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference (Julia NNop) cannot run here: no Julia toolchain and every kernel is cpu=false; "
@@ -225,9 +246,7 @@ def run_ours(args):
 
     import nnop
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, local, world = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -241,7 +260,7 @@ def run_ours(args):
     E, L, H, B, causal = CFG["E"], CFG["L"], CFG["H"], CFG["B"], CFG["causal"]
     dt = torch.bfloat16
     g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
+    g.manual_seed(rank_seed(rank))
     q = torch.randn(B, H, L, E, device=dev, dtype=dt, generator=g)
     k = torch.randn(B, H, L, E, device=dev, dtype=dt, generator=g)
     v = torch.randn(B, H, L, E, device=dev, dtype=dt, generator=g)
@@ -272,6 +291,8 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    from nnop._lib import lib as _nnlib
+    _nnlib.nnop_kernel_timing(1)   # CUDA events around the attention kernels, on their stream
     t_start.record(stream)
     for i in range(K):
         ev[3 * i].record(stream)
@@ -281,18 +302,23 @@ def run_ours(args):
         ev[3 * i + 2].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
+    _nnlib.nnop_kernel_timing(0)
     barrier()
     clk = clocks.stop()
+    import ctypes as _C
+    kern_ms = []
+    for which in (0, 1):
+        tot, cnt = _C.c_double(0.0), _C.c_int(0)
+        _nnlib.nnop_kernel_timing_read(which, _C.byref(tot), _C.byref(cnt))
+        kern_ms.append(tot.value / cnt.value if cnt.value else float("nan"))
     ms_local = t_start.elapsed_time(t_end) / K
     fwd_ms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(K)) / K
     bwd_ms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(K)) / K
-    t = torch.tensor([ms_local, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, fwd_ms, bwd_ms = (float(x) for x in t.tolist())
+    ms, fwd_ms, bwd_ms, fwd_kern_ms, bwd_kern_ms = max_over_ranks(
+        [ms_local, fwd_ms, bwd_ms, kern_ms[0], kern_ms[1]], dev, world)
 
     fwd_f, bwd_f = cfg_flops(B, H, L, E, causal)
-    value = (fwd_f + bwd_f) * world / (ms / 1e3) / 1e12
+    value = job_tflops(fwd_f + bwd_f, world, ms)
 
     # ---- end to end through the public API with host buffers (pinned).
     # Every step copies its inputs host->device and its gradients device->host;
@@ -346,22 +372,28 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    te = torch.tensor([e0.elapsed_time(e1) / Ke], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
-    e2e_value = (fwd_f + bwd_f) * world / (e2e_ms / 1e3) / 1e12
+    e2e_ms = max_over_ranks([e0.elapsed_time(e1) / Ke], dev, world)[0]
+    e2e_value = job_tflops(fwd_f + bwd_f, world, e2e_ms)
 
     hbm, tc, src = peaks()
-    bwd_bytes = cfg_bytes(B, H, L, E, causal)[1]
-    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    # Dominant kernel: fa_bwd_sm100_kernel (largest share of the launch list,
+    # profiles/fa_config2_launches_tcgen05.md), timed live with CUDA events on
+    # its stream.  Algorithmic bytes per launch: pair tiles read and dS tiles
+    # written (causal half each), q, k, v, dO read, lse and delta read, dk, dv
+    # written, the fp32 dq accumulator read and written once.
+    c = 0.5 if causal else 1.0
+    kern_bytes = (2 * c * B * H * L * L * 2 + 4 * B * H * L * E * 2 + 2 * B * H * L * 4 + 2 * B * H * L * E * 2
+                  + 2 * B * H * L * E * 4)
+    achieved = kern_bytes / (bwd_kern_ms / 1e3) / 1e9
     roofline = {
-        "kernel": "flash_attention_bwd call (preprocess, fa_bwd_sm100_kernel, dq convert, dpair_from_tiles)",
-        "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-        "peak_source": f"{src} hbm_gbs", "traffic": None,
-        "algorithmic_bytes_per_launch": bwd_bytes, "launch_ms": bwd_ms,
-        "tensor_frac_of_step": (fwd_f + bwd_f) / (ms / 1e3) / 1e12 / tc,
-        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "kernel": "fa_bwd_sm100_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+        "frac": achieved / hbm, "peak_source": f"{src} hbm_gbs (burst copy)",
+        # dram__bytes_read.sum + dram__bytes_write.sum of one launch at B=1 (ncu,
+        # profiles/fa_bwd_sm100_config2_b1.md) x 8 batches: traffic grows with the batch
+        "traffic": TRAFFIC_BWD_B1 * B,
+        "algorithmic_bytes_per_launch": kern_bytes, "launch_ms": bwd_kern_ms,
+        "tensor_frac": bwd_f / (bwd_kern_ms / 1e3) / 1e12 / tc, "tensor_peak_tflops": tc,
+        "fwd_kernel_ms": fwd_kern_ms, "fwd_call_ms": fwd_ms, "bwd_call_ms": bwd_ms,
     }
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

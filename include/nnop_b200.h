@@ -70,6 +70,19 @@ const char* nnop_status_string(int status);
  */
 int nnop_device_wait_timeouts(void);
 
+/*
+ * Launch timing of the tensor-core attention kernels (no counterpart in the
+ * reference; for benchmarks and profiles).  nnop_kernel_timing(1) makes every
+ * following forward / backward call record CUDA events on its stream around
+ * its attention kernel (up to 256 launches; later ones are not timed);
+ * nnop_kernel_timing(0) stops.  nnop_kernel_timing_read(which, &ms, &count)
+ * waits for the recorded events, returns the summed milliseconds and number
+ * of timed launches of the forward (which = 0) or backward (which = 1) kernel
+ * on the current device, and clears that record.
+ */
+void nnop_kernel_timing(int enable);
+int nnop_kernel_timing_read(int which, double* total_ms, int* count);
+
 /* --------------------------------------------------------------------------
  * Flash attention
  * -------------------------------------------------------------------------- */

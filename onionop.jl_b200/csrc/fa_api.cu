@@ -4,6 +4,7 @@
 #include "fa_common.cuh"
 
 #include <cstdlib>
+#include <mutex>
 #include <type_traits>
 
 namespace nnop {
@@ -68,6 +69,42 @@ int check_dims(int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_
 // bf16/f16, E = 64, at most 64 heads (the re-layout stages [8][128][H] blocks).
 bool pair_tiles_path(int64_t E, int64_t QH, int dtype) {
     return !force_mma() && (dtype == NNOP_BF16 || dtype == NNOP_F16) && E == 64 && QH <= 64;
+}
+
+// Optional CUDA-event timing of the attention kernels (nnop_kernel_timing).
+struct KernelTimer {
+    static constexpr int kMax = 256;
+    std::mutex mu;
+    bool on = false;
+    int dev[2][kMax];
+    int n[2] = {0, 0};
+    cudaEvent_t ev[2][kMax][2];
+    bool made = false;
+};
+KernelTimer& timer() {
+    static KernelTimer t;
+    return t;
+}
+// Records the start event of a timed launch; returns the slot or -1.
+int timer_begin(int which, cudaStream_t s) {
+    KernelTimer& t = timer();
+    std::lock_guard<std::mutex> lock(t.mu);
+    if (!t.on || t.n[which] >= KernelTimer::kMax) return -1;
+    if (!t.made) {
+        for (int w = 0; w < 2; ++w)
+            for (int i = 0; i < KernelTimer::kMax; ++i)
+                for (int e = 0; e < 2; ++e)
+                    if (cudaEventCreate(&t.ev[w][i][e]) != cudaSuccess) return -1;
+        t.made = true;
+    }
+    const int slot = t.n[which]++;
+    cudaGetDevice(&t.dev[which][slot]);
+    cudaEventRecord(t.ev[which][slot][0], s);
+    return slot;
+}
+void timer_end(int which, int slot, cudaStream_t s) {
+    if (slot < 0) return;
+    cudaEventRecord(timer().ev[which][slot][1], s);
 }
 
 struct BwdWorkspace {
@@ -146,7 +183,9 @@ int bwd_16bit(fa::Params& p, const BwdWorkspace& ws, const void* fwd_tiles, int6
                                                causal, s);
             if (st) return st;
         }
+        const int slot = timer_begin(1, s);
         st = fa::sm100_bwd(p, tiles, ws.ds_tiles, dtype, causal, s);
+        timer_end(1, slot, s);
     } else {
         st = fa::mma_bwd<T>(p, causal, s);
     }
@@ -165,6 +204,36 @@ int bwd_16bit(fa::Params& p, const BwdWorkspace& ws, const void* fwd_tiles, int6
 using namespace nnop;
 
 extern "C" {
+
+void nnop_kernel_timing(int enable) {
+    KernelTimer& t = timer();
+    std::lock_guard<std::mutex> lock(t.mu);
+    t.on = enable != 0;
+}
+
+int nnop_kernel_timing_read(int which, double* total_ms, int* count) {
+    if ((which != 0 && which != 1) || !total_ms || !count)
+        return fail(NNOP_ERR_ARG, "kernel_timing_read: which must be 0 or 1, outputs non-NULL");
+    KernelTimer& t = timer();
+    std::lock_guard<std::mutex> lock(t.mu);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    double sum = 0;
+    int c = 0;
+    for (int i = 0; i < t.n[which]; ++i) {
+        if (t.dev[which][i] != dev) continue;
+        float ms = 0.f;
+        if (cudaEventSynchronize(t.ev[which][i][1]) != cudaSuccess ||
+            cudaEventElapsedTime(&ms, t.ev[which][i][0], t.ev[which][i][1]) != cudaSuccess)
+            return fail(NNOP_ERR_CUDA, "kernel_timing_read: event query failed");
+        sum += ms;
+        ++c;
+    }
+    t.n[which] = 0;
+    *total_ms = sum;
+    *count = c;
+    return NNOP_OK;
+}
 
 int nnop_device_wait_timeouts(void) {
     const int f = fa::sm100_fwd_timeouts();
@@ -218,7 +287,10 @@ int nnop_flash_attention_fwd(const void* q, const void* k, const void* v, const 
                                                                  KL, (int)QH, (int)B, causal != 0, s);
                     if (st) return st;
                 }
-                return fa::sm100_fwd(p, workspace, dtype, causal != 0, s);
+                const int slot = timer_begin(0, s);
+                st = fa::sm100_fwd(p, workspace, dtype, causal != 0, s);
+                timer_end(0, slot, s);
+                return st;
             }
             return bf ? fa::mma_fwd<__nv_bfloat16>(p, causal != 0, s) : fa::mma_fwd<__half>(p, causal != 0, s);
         }

@@ -29,6 +29,8 @@ SIGNATURES = {
     "nnop_last_error": (C.c_char_p, []),
     "nnop_status_string": (C.c_char_p, [_int]),
     "nnop_device_wait_timeouts": (_int, []),
+    "nnop_kernel_timing": (None, [_int]),
+    "nnop_kernel_timing_read": (_int, [_int, C.POINTER(C.c_double), C.POINTER(_int)]),
     "nnop_flash_attention_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                         _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "nnop_flash_attention_fwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int, _int]),
