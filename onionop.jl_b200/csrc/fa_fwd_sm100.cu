@@ -44,6 +44,7 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 2;
+constexpr int kPairSlots = 3;        // pair tiles in flight (loaded two key tiles ahead)
 constexpr int kThreads = 256;
 constexpr int kMaxKeyWords = 2048;   // validity bits for up to 65536 keys
 constexpr unsigned kFull = 0xffffffffu;
@@ -57,10 +58,10 @@ enum Bar {
     kPFull = 9,      // +buffer
     kOFinal = 11,
     kOStep = 12,
-    kPairFull = 13,  // +buffer (TMA -> MMA)
-    kPairEmpty = 15, // +buffer (its UMMAs retired -> producer)
-    kMmaDone = 17,   // MMA warp's own "all my MMAs retired" barrier
-    kNumBars = 18
+    kPairFull = 13,  // +slot (TMA -> MMA)
+    kPairEmpty = 16, // +slot (its UMMAs retired -> producer)
+    kMmaDone = 19,   // MMA warp's own "all my MMAs retired" barrier
+    kNumBars = 20
 };
 
 template <int E, bool PAIR>
@@ -72,7 +73,7 @@ struct Layout {
     static constexpr int kV = kK + kStages * kKVBytes;
     static constexpr int kPairBytes = PAIR ? kBN * kBM * 2 : 0;
     static constexpr int kPair = kV + kStages * kKVBytes;
-    static constexpr int kEye = kPair + 2 * kPairBytes;         // shifted identity (1024-aligned)
+    static constexpr int kEye = kPair + kPairSlots * kPairBytes;  // shifted identity (1024-aligned)
     static constexpr int kBits = kEye + (PAIR ? kEyeBytes : 0); // kMaxKeyWords uint32
     static constexpr int kBar = kBits + kMaxKeyWords * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
@@ -149,6 +150,8 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars[kSFull + i], 1);
             mbar_init(&bars[kPFull + i], 128);
+        }
+        for (int i = 0; i < kPairSlots; ++i) {
             mbar_init(&bars[kPairFull + i], 1);
             mbar_init(&bars[kPairEmpty + i], 1);
         }
@@ -186,11 +189,25 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
             for (int half = 0; half < E / 64; ++half)
                 tma_load_3d(smem + L::kQ + half * kBM * 128, &tm_q, &bars[kQFull], half * 64, (int)q0, bh_q);
-            int issued = 0;
-            for (int j = 0; j < n_kt; ++j) {
+            int issued = 0, pair_issued = 0;
+            // pair tile of key tile j into slot j % 3 once tile j - 3 has been consumed
+            auto load_pair = [&](int j) -> bool {
+                const int slot = j % kPairSlots;
+                if (j >= kPairSlots && !wait(&bars[kPairEmpty + slot], ((j / kPairSlots) - 1) & 1, ab, 2))
+                    return false;
+                mbar_expect_tx(&bars[kPairFull + slot], L::kPairBytes);
+#pragma unroll
+                for (int half = 0; half < 2; ++half)
+                    tma_load_4d(smem + L::kPair + slot * L::kPairBytes + half * kBN * 128, &tm_pair,
+                                &bars[kPairFull + slot], half * 64, j * kBN, qt, bh_q);
+                pair_issued = j + 1;
+                return true;
+            };
+            bool run = true;
+            if (PAIR) run = load_pair(0) && (n_kt < 2 || load_pair(1));
+            for (int j = 0; run && j < n_kt; ++j) {
                 const int s = j % kStages;
                 if (j >= kStages && !wait(&bars[kKVEmpty + s], ((j / kStages) - 1) & 1, ab, 1)) break;
-                if (PAIR && j >= 2 && !wait(&bars[kPairEmpty + (j & 1)], ((j >> 1) - 1) & 1, ab, 2)) break;
                 issued = j + 1;
                 const int k0 = j * kBN;
                 mbar_expect_tx(&bars[kKFull + s], L::kKVBytes);
@@ -203,13 +220,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 for (int half = 0; half < E / 64; ++half)
                     tma_load_3d(smem + L::kV + s * L::kKVBytes + half * kBN * 128, &tm_v, &bars[kVFull + s],
                                 half * 64, k0, bh_k);
-                if (PAIR) {
-                    mbar_expect_tx(&bars[kPairFull + (j & 1)], L::kPairBytes);
-#pragma unroll
-                    for (int half = 0; half < 2; ++half)
-                        tma_load_4d(smem + L::kPair + (j & 1) * L::kPairBytes + half * kBN * 128, &tm_pair,
-                                    &bars[kPairFull + (j & 1)], half * 64, k0, qt, bh_q);
-                }
+                if (PAIR && j + 2 < n_kt) run = load_pair(j + 2);
             }
             // Copies still in flight must land before the CTA can exit (they
             // have, unless a consumer gave up): bounded waits on the last ones.
@@ -217,8 +228,9 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             for (int j = issued - kStages < 0 ? 0 : issued - kStages; j < issued; ++j) {
                 wait(&bars[kKFull + j % kStages], (j / kStages) & 1, ab, 4);
                 wait(&bars[kVFull + j % kStages], (j / kStages) & 1, ab, 5);
-                if (PAIR) wait(&bars[kPairFull + (j & 1)], (j >> 1) & 1, ab, 6);
             }
+            for (int j = pair_issued - kPairSlots < 0 ? 0 : pair_issued - kPairSlots; j < pair_issued; ++j)
+                wait(&bars[kPairFull + j % kPairSlots], (j / kPairSlots) & 1, ab, 6);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -230,7 +242,7 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         auto issue_s = [&](int j) -> bool {
             const int s = j % kStages;
             if (!wait_warp(&bars[kKFull + s], (j / kStages) & 1, ab, 8)) return false;
-            if (PAIR && !wait_warp(&bars[kPairFull + (j & 1)], (j >> 1) & 1, ab, 12)) return false;
+            if (PAIR && !wait_warp(&bars[kPairFull + j % kPairSlots], (j / kPairSlots) & 1, ab, 12)) return false;
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t sK = smem_u32(smem + L::kK + s * L::kKVBytes);
@@ -243,12 +255,12 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 }
                 if (PAIR) {
                     // S += c·I·pairᵀ: B = pair tile [key][query], K-major over queries
-                    const uint32_t sP = smem_u32(smem + L::kPair + (j & 1) * L::kPairBytes);
+                    const uint32_t sP = smem_u32(smem + L::kPair + (j % kPairSlots) * L::kPairBytes);
 #pragma unroll
                     for (int kk = 0; kk < kBM / 16; ++kk)
                         umma_ss(d, desc_k_sw128(eye_step(sEye, kk)),
                                 desc_k_sw128(sP + (kk / 4) * kBN * 128 + (kk % 4) * 32), idesc_s, 1u);
-                    umma_commit(&bars[kPairEmpty + (j & 1)]);
+                    umma_commit(&bars[kPairEmpty + j % kPairSlots]);
                 }
                 umma_commit(&bars[kSFull + (j & 1)]);
             }
