@@ -27,16 +27,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ bool elect_one() {
-    uint32_t pred = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "elect.sync _|p, 0xffffffff;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(pred));
-    return pred != 0;
-}
-
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
@@ -86,69 +76,6 @@ __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, volatile in
     }
 }
 
-// Cluster-scope variant: the phase is completed by other CTAs of the cluster
-// (remote arrives, st.async complete_tx), so the acquire is at cluster scope.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort = nullptr,
-                                             int site = 0) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (true) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (abort && *abort) return false;
-        if (clock64() - t0 > kWaitCycles) return wait_give_up(abort, site);
-    }
-}
-
-// ------------------------------------------------------------------ cluster
-// Distributed shared memory between the CTAs of a thread-block cluster.  Only
-// plain peer stores / arrives are used (no TMA multicast).
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-    return r;
-}
-// shared::cluster address of `local_addr` (a shared::cta address) in CTA `rank`.
-__device__ __forceinline__ uint32_t mapa(uint32_t local_addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local_addr), "r"(rank));
-    return r;
-}
-// 16-byte store into a peer CTA's shared memory that completes `bytes` of the
-// transaction count of the peer's mbarrier.
-__device__ __forceinline__ void st_async16(uint32_t remote_addr, const uint4& v, uint32_t remote_bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];\n" ::"r"(
-                     remote_addr),
-                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(remote_bar)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(remote_bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx_cluster(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-// Whole-cluster barrier (every thread of every CTA of the cluster).
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 // ------------------------------------------------------------------ TMA
 // Tensor maps are passed as __grid_constant__ kernel parameters.
 __device__ __forceinline__ void tma_prefetch(const void* tmap) {
@@ -171,16 +98,9 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
-// Tiled store shared::cta -> global through a tensor map; completion is
-// tracked by bulk groups (commit, then wait until the source has been read
-// or the writes are done).
-__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(tmap),
-        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
-        : "memory");
-}
-// Tiled reduce-add shared::cta -> global (element type from the tensor map).
+// Tiled store and reduce-add shared::cta -> global through a tensor map (the
+// element type comes from the map); completion is tracked by bulk groups:
+// commit, then wait until the source has been read or the writes are done.
 __device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
     asm volatile(
         "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(tmap),
