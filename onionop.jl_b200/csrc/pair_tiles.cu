@@ -174,11 +174,17 @@ __global__ void __launch_bounds__(kTB) dpair_from_tiles_kernel(const T* __restri
 
 // ---------------------------------------------------------------------------
 // Fast path for H = 8·CQ heads, CQ in {1, 2, 4, 8}: the block's key rows sit in
-// shared memory as 16-byte chunks (CQ per query), chunk L of a row stored at
-// swz(L); a thread moves two heads × 8 queries at a time with 32-bit shared
-// accesses and byte permutes.  The swizzle spreads the 8/CQ query pieces a
-// warp touches at once over distinct bank groups, so neither the 16-byte
-// fills nor the 32-bit gathers conflict.
+// shared memory as 16-byte chunks (CQ per query: 8 heads each), chunk L of a
+// row stored at swz(L); a thread moves 8 heads × 8 queries at a time: eight
+// 16-byte shared accesses and an 8×8 transpose of 16-bit values in registers
+// (byte permutes).  The swizzle spreads the query pieces a warp touches at
+// once over distinct bank groups, so the 16-byte accesses need the minimum
+// four wavefronts.
+// word i of a 16-byte vector (i a compile-time constant after unrolling)
+__device__ __forceinline__ uint32_t word(const uint4& u, int i) {
+    return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
+}
+
 template <int CQ>
 __device__ __forceinline__ int swz(int L) {
     constexpr int NV = 8 / CQ;
@@ -211,7 +217,6 @@ __global__ void __launch_bounds__(kTB, 3) pair_tiles_fast_kernel(const T* __rest
     constexpr int RC = kTile * CQ;   // 16-byte chunks per key row
     extern __shared__ __align__(16) uint8_t sm_raw[];
     uint4* s4 = reinterpret_cast<uint4*>(sm_raw);          // [8][RC] swizzled
-    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm_raw);
     const int c = blockIdx.x;
     const int64_t g = blockIdx.y;
     const int b = blockIdx.z;
@@ -243,28 +248,27 @@ __global__ void __launch_bounds__(kTB, 3) pair_tiles_fast_kernel(const T* __rest
         }
     }
     __syncthreads();
-    // thread -> (key kk, 8-query piece v, head pair hp), head pairs fastest
-    constexpr int kPieces = kKeys * (kTile / 8) * (H / 2);
-#pragma unroll 2
-    for (int x = threadIdx.x; x < kPieces; x += kTB) {
-        const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
-        uint32_t w[8];
+    // thread -> (key kk, 8-query piece v, head octet ho), octets fastest
+    constexpr int kItems = kKeys * (kTile / 8) * CQ;
+    for (int x = threadIdx.x; x < kItems; x += kTB) {
+        const int ho = x % CQ, v = (x / CQ) % (kTile / 8), kk = x / (CQ * (kTile / 8));
+        uint4 r[8];   // r[e]: heads 8ho..8ho+7 of query v*8+e
 #pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = s32[(kk * RC + swz<CQ>((v * 8 + e) * CQ + hp / 4)) * 4 + hp % 4];
-        uint32_t lo[4], hi[4];
+        for (int e = 0; e < 8; ++e) r[e] = s4[kk * RC + swz<CQ>((v * 8 + e) * CQ + ho)];
+        T* dst = out + ((((int64_t)b * H + 8 * ho) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            lo[j] = finite2<T>(__byte_perm(w[2 * j], w[2 * j + 1], 0x5410));
-            hi[j] = finite2<T>(__byte_perm(w[2 * j], w[2 * j + 1], 0x7632));
+        for (int j = 0; j < 8; ++j) {   // head 8ho+j: queries (2m, 2m+1) in word m
+            const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
+            uint32_t o[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) o[m] = finite2<T>(__byte_perm(word(r[2 * m], j >> 1), word(r[2 * m + 1], j >> 1), sel));
+            __stcs(reinterpret_cast<uint4*>(dst + (int64_t)j * klp * qlp), make_uint4(o[0], o[1], o[2], o[3]));
         }
-        T* dst = out + ((((int64_t)b * H + 2 * hp) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
-        __stcs(reinterpret_cast<uint4*>(dst), make_uint4(lo[0], lo[1], lo[2], lo[3]));
-        __stcs(reinterpret_cast<uint4*>(dst + klp * qlp), make_uint4(hi[0], hi[1], hi[2], hi[3]));
     }
 }
 
 template <typename T, int CQ>
-__global__ void __launch_bounds__(kTB, 3) dpair_from_tiles_fast_kernel(const T* __restrict__ tiles,
+__global__ void __launch_bounds__(kTB, CQ >= 4 ? 2 : 3) dpair_from_tiles_fast_kernel(const T* __restrict__ tiles,
                                                                     T* __restrict__ dpair,
                                                                     const int* __restrict__ kv_len, int64_t QL,
                                                                     int64_t KL, int64_t qlp, int64_t klp,
@@ -273,41 +277,29 @@ __global__ void __launch_bounds__(kTB, 3) dpair_from_tiles_fast_kernel(const T* 
     constexpr int RC = kTile * CQ;
     extern __shared__ __align__(16) uint8_t sm_raw[];
     uint4* s4 = reinterpret_cast<uint4*>(sm_raw);
-    uint32_t* s32 = reinterpret_cast<uint32_t*>(sm_raw);
     const int c = blockIdx.x;
     const int64_t g = blockIdx.y;
     const int b = blockIdx.z;
     const int64_t i0 = (int64_t)c * kTile;
     const bool vis = visited(c, g, b, kv_len, causal);
     if (vis) {
-        constexpr int kPieces = kKeys * (kTile / 8) * (H / 2);
-        constexpr int kBatch = 4;   // pieces in flight per thread
-#pragma unroll 1
-        for (int x0 = 0; x0 < kPieces; x0 += kBatch * kTB) {
-            uint4 a[kBatch], bq[kBatch];
+        // thread -> (key kk, 8-query piece v, head octet ho): eight 16-byte
+        // loads (one per head) in flight, transposed into eight query chunks
+        constexpr int kItems = kKeys * (kTile / 8) * CQ;
+        for (int x = threadIdx.x; x < kItems; x += kTB) {
+            const int ho = x % CQ, v = (x / CQ) % (kTile / 8), kk = x / (CQ * (kTile / 8));
+            const T* p0 = tiles + ((((int64_t)b * H + 8 * ho) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
+            uint4 in[8];   // in[j]: queries v*8..v*8+7 of head 8ho+j
 #pragma unroll
-            for (int t = 0; t < kBatch; ++t) {
-                const int x = x0 + t * kTB + threadIdx.x;
-                if (x < kPieces) {
-                    const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
-                    const T* p0 =
-                        tiles + ((((int64_t)b * H + 2 * hp) * (qlp / kTile) + c) * klp + g * kKeys + kk) * kTile + v * 8;
-                    a[t] = __ldcs(reinterpret_cast<const uint4*>(p0));
-                    bq[t] = __ldcs(reinterpret_cast<const uint4*>(p0 + klp * qlp));
-                }
-            }
+            for (int j = 0; j < 8; ++j) in[j] = __ldcs(reinterpret_cast<const uint4*>(p0 + (int64_t)j * klp * qlp));
 #pragma unroll
-            for (int t = 0; t < kBatch; ++t) {
-                const int x = x0 + t * kTB + threadIdx.x;
-                if (x < kPieces) {
-                    const int hp = x % (H / 2), v = (x / (H / 2)) % (kTile / 8), kk = x / ((H / 2) * (kTile / 8));
-                    const uint32_t aw[4] = {a[t].x, a[t].y, a[t].z, a[t].w};
-                    const uint32_t bw[4] = {bq[t].x, bq[t].y, bq[t].z, bq[t].w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        s32[(kk * RC + swz<CQ>((v * 8 + e) * CQ + hp / 4)) * 4 + hp % 4] =
-                            __byte_perm(aw[e / 2], bw[e / 2], (e & 1) ? 0x7632 : 0x5410);
-                }
+            for (int e = 0; e < 8; ++e) {   // query v*8+e: heads (2w, 2w+1) in word w
+                const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+                s4[kk * RC + swz<CQ>((v * 8 + e) * CQ + ho)] =
+                    make_uint4(__byte_perm(word(in[0], e >> 1), word(in[1], e >> 1), sel),
+                               __byte_perm(word(in[2], e >> 1), word(in[3], e >> 1), sel),
+                               __byte_perm(word(in[4], e >> 1), word(in[5], e >> 1), sel),
+                               __byte_perm(word(in[6], e >> 1), word(in[7], e >> 1), sel));
             }
         }
         __syncthreads();
