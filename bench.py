@@ -239,6 +239,78 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+# --------------------------------------------------------------- memory-bound ops
+def run_memory_suite(args):
+    """BASELINE config 5 (rms_norm / layer_norm on x (4096, 65536) bf16 and fp32,
+    online_softmax on x (8192, 16384) fp32) and the RoPE of config 3 (q 32 heads,
+    k 8 heads, L = 8192, E = 128, bf16), fwd and bwd, on one GPU: achieved HBM
+    GB/s from the algorithmic bytes (each tensor read or written once) and CUDA
+    events over K launches; every input is larger than L2."""
+    import torch
+
+    import nnop
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, _, src = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    K, W = max(args.steps, 3), max(args.warmup, 3)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / K
+
+    rows = {}
+
+    def add(name, nbytes, ms):
+        rows[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / hbm}
+
+    emb, n = 4096, 65536
+    for dt, tag in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+        es = 2 if dt == torch.bfloat16 else 4
+        x = torch.randn(n, emb, device=dev, dtype=dt, generator=g)
+        w = (1 + 0.1 * torch.randn(emb, device=dev, generator=g)).to(dt)
+        b = (0.1 * torch.randn(emb, device=dev, generator=g)).to(dt)
+        dy = torch.randn(n, emb, device=dev, dtype=dt, generator=g)
+        y, rstd = nnop._rms_norm(x, w)
+        add(f"rms_norm_fwd_{tag}", 2 * n * emb * es, timed(lambda: nnop._rms_norm(x, w)))
+        add(f"rms_norm_bwd_{tag}", 3 * n * emb * es, timed(lambda: nnop.grad_rms_norm(dy, rstd, x, w)))
+        y, mu, rs = nnop._layer_norm(x, w, b)
+        add(f"layer_norm_fwd_{tag}", 2 * n * emb * es, timed(lambda: nnop._layer_norm(x, w, b)))
+        add(f"layer_norm_bwd_{tag}", 3 * n * emb * es, timed(lambda: nnop.grad_layer_norm(dy, mu, rs, x, w)))
+        del x, dy, y
+        torch.cuda.empty_cache()
+    x = 2 * torch.randn(16384, 8192, device=dev, generator=g)
+    y = nnop.online_softmax(x)
+    dy = torch.randn_like(x)
+    add("online_softmax_fwd_f32", 2 * x.numel() * 4, timed(lambda: nnop.online_softmax(x)))
+    add("online_softmax_bwd_f32", 3 * x.numel() * 4, timed(lambda: nnop.grad_online_softmax(dy, y)))
+    del x, y, dy
+    torch.cuda.empty_cache()
+    B, QH, KH, L, E = 4, 32, 8, 8192, 128
+    q = torch.randn(B, QH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    pos = torch.arange(L, device=dev, dtype=torch.float32).repeat(B, 1)
+    cos, sin = nnop.LlamaRotaryEmbedding(E)(pos)
+    rb = 2 * (q.numel() + k.numel()) * 2 + 2 * cos.numel() * 4
+    add("llama_rope_fwd_bf16", rb, timed(lambda: nnop.llama_rope(q, k, cos=cos, sin=sin)))
+    add("llama_rope_bwd_bf16", rb, timed(lambda: nnop.grad_llama_rope(q, k, cos=cos, sin=sin)))
+    out = {"suite": "memory", "unit": "GB/s", "peak": hbm, "peak_source": f"{src} hbm_gbs", "steps": K,
+           "warmup": W, "ops": rows,
+           "config": {"norms": "x (4096, 65536) Julia = [65536][4096] rows, w (and b) (4096,)",
+                      "softmax": "x (8192, 16384) fp32, dim 1", "rope": "q (128, 8192, 32, 4), k (128, 8192, 8, 4) bf16"}}
+    print(json.dumps(out), flush=True)
+
+
 # --------------------------------------------------------------- GPU arm
 def run_ours(args):
     import torch
@@ -433,6 +505,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--suite", default="attention", choices=["attention", "memory"],
+                    help="memory: the norm / softmax / RoPE sweep (BASELINE configs 5 and 3's RoPE) on one GPU")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override, for small profiler captures (the headline uses 8)")
     args = ap.parse_args()
@@ -440,6 +514,8 @@ def main():
         CFG["B"] = args.batch
     if args.impl == "reference":
         run_reference(args)
+    elif args.suite == "memory":
+        run_memory_suite(args)
     else:
         run_ours(args)
 

@@ -114,17 +114,29 @@ rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __res
                 for (int e = 0; e < VEC; ++e) wo[i][e] = wv[e] + offset;
             }
         }
+        // the next row's x and dy are loaded while this row is reduced and written
+        Vec<T, VEC> xn_[NV], dn_[NV];
+        auto load_row = [&](int64_t row) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (row < n && idx < nvec) {
+                    xn_[i] = ldg_stream<T, VEC>(x + row * (int64_t)emb + idx * VEC);
+                    dn_[i] = ldg_stream<T, VEC>(dy + row * (int64_t)emb + idx * VEC);
+                }
+            }
+        };
+        load_row(blockIdx.x);
         for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
-            const T* xr = x + row * (int64_t)emb;
-            const T* dr = dy + row * (int64_t)emb;
             Vec<T, VEC> xc[NV], dc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) { xc[i] = xn_[i]; dc[i] = dn_[i]; }
+            load_row(row + gridDim.x);
             float dd[1] = {0.f};
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 const int idx = tid + i * nt;
                 if (idx < nvec) {
-                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
-                    dc[i] = ldg_stream<T, VEC>(dr + idx * VEC);
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) dd[0] += to_f(dc[i].v[e]) * wo[i][e] * to_f(xc[i].v[e]);
                 }
@@ -297,18 +309,30 @@ ln_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __rest
             for (int e = 0; e < VEC; ++e) { wv[i][e] = 0.f; dwa[i][e] = 0.f; dba[i][e] = 0.f; }
             if (idx < nvec) load_vec<T, VEC>(wv[i], w + idx * VEC);
         }
+        // the next row's x and dy are loaded while this row is reduced and written
+        Vec<T, VEC> xn_[NV], dn_[NV];
+        auto load_row = [&](int64_t row) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (row < n && idx < nvec) {
+                    xn_[i] = ldg_stream<T, VEC>(x + row * (int64_t)emb + idx * VEC);
+                    dn_[i] = ldg_stream<T, VEC>(dy + row * (int64_t)emb + idx * VEC);
+                }
+            }
+        };
+        load_row(blockIdx.x);
         for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
-            const T* xr = x + row * (int64_t)emb;
-            const T* dr = dy + row * (int64_t)emb;
             const float mu = mean[row], r = rstd[row];
             Vec<T, VEC> xc[NV], dc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) { xc[i] = xn_[i]; dc[i] = dn_[i]; }
+            load_row(row + gridDim.x);
             float c[2] = {0.f, 0.f};
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 const int idx = tid + i * nt;
                 if (idx < nvec) {
-                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
-                    dc[i] = ldg_stream<T, VEC>(dr + idx * VEC);
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) {
                         const float xn = (to_f(xc[i].v[e]) - mu) * r;
@@ -410,7 +434,10 @@ __global__ void reduce_partials_kernel(const float* __restrict__ partial, TO* __
 
 // ---------------------------------------------------------------- dispatch
 // Picks the 16-byte vector path when every row starts 16-byte aligned, and the
-// number of cached vectors per thread from the row length.
+// number of cached vectors per thread from the row length.  `max_elems`
+// bounds the elements a thread caches: the backward kernels also keep per-thread
+// dw/db accumulators for their columns, and beyond 32 elements those spill, so
+// longer rows take the uncached path (x, dy re-read, mostly from L2).
 struct RowPlan {
     bool vec;
     int block;
@@ -418,7 +445,7 @@ struct RowPlan {
 };
 
 template <typename T>
-RowPlan plan_rows(int emb, std::initializer_list<const void*> ptrs) {
+RowPlan plan_rows(int emb, std::initializer_list<const void*> ptrs, int max_elems = 1 << 30) {
     constexpr int V = 16 / sizeof(T);
     bool vec = (emb % V == 0);
     for (const void* p : ptrs) vec = vec && (p == nullptr || aligned16(p));
@@ -429,7 +456,7 @@ RowPlan plan_rows(int emb, std::initializer_list<const void*> ptrs) {
     const int per = (nvec + block - 1) / block;
     int nv = 1;
     while (nv < per) nv *= 2;
-    if (nv > kMaxNV) nv = 0;
+    if (nv > kMaxNV || nv * (vec ? V : 1) > max_elems) nv = 0;
     return {vec, block, nv};
 }
 
@@ -522,7 +549,7 @@ int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w, const float*
     float* partial = (float*)workspace;
     int parts = 0;
     NNOP_DISPATCH_DTYPE(dtype, T, {
-        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx});
+        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
                 auto kern = rms_bwd_kernel<T, VC, NVC>;
@@ -583,7 +610,7 @@ int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w, const floa
     float* partial = (float*)workspace;
     int parts = 0;
     NNOP_DISPATCH_DTYPE(dtype, T, {
-        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx});
+        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
                 auto kern = ln_bwd_kernel<T, VC, NVC>;
@@ -670,7 +697,7 @@ int nnop_rms_norm_bwd_noalloc(const void* dy, const void* x, const void* w, cons
     const int64_t max_parts = kNoAllocScratchFloats / emb;
     int parts = 0;
     NNOP_DISPATCH_DTYPE(dtype, T, {
-        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx});
+        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
                 auto kern = rms_bwd_kernel<T, VC, NVC>;
