@@ -6,7 +6,9 @@
 // Design (HBM-bound, 2·N·s bytes forward, 3·N·s backward):
 // * one CTA normalises one row (a Julia column of length emb) at a time; each
 //   thread holds its slice of the row in registers as raw 16-byte vectors, so x
-//   (and dy) are read from HBM exactly once;
+//   (and dy) are read from HBM exactly once; CTAs that walk several rows load
+//   the next row's vectors while the current row is reduced and written (the
+//   backward, and the 16-bit forward, which runs persistent CTAs);
 // * reductions are warp shuffles plus one shared-memory stage;
 // * the backward runs a persistent grid (SM count x resident CTAs); a thread
 //   owns the same columns for every row it visits, so dw/db accumulate in
@@ -34,20 +36,31 @@ rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__
     __shared__ float red[32];
     const int nvec = emb / VEC;
     const int tid = threadIdx.x, nt = blockDim.x;
-    for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
-        const T* xr = x + row * (int64_t)emb;
-        T* yr = y + row * (int64_t)emb;
-        float ss[1] = {0.f};
-        if constexpr (NV > 0) {
+    if constexpr (NV > 0) {
+        // persistent CTAs; the next row is loaded while this one is reduced and written
+        Vec<T, VEC> xn_[NV];
+        auto load_row = [&](int64_t row) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (row < n && idx < nvec) xn_[i] = ldg_stream<T, VEC>(x + row * (int64_t)emb + idx * VEC);
+            }
+        };
+        load_row(blockIdx.x);
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            T* yr = y + row * (int64_t)emb;
             Vec<T, VEC> xc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) xc[i] = xn_[i];
+            load_row(row + gridDim.x);
+            float ss[1] = {0.f};
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 const int idx = tid + i * nt;
                 if (idx < nvec) {
-                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) {
-                        float f = to_f(xc[i].v[e]);
+                        const float f = to_f(xc[i].v[e]);
                         ss[0] += f * f;
                     }
                 }
@@ -66,7 +79,12 @@ rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__
                     store_vec<T, VEC>(yr + idx * VEC, o);
                 }
             }
-        } else {
+        }
+    } else {
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            const T* xr = x + row * (int64_t)emb;
+            T* yr = y + row * (int64_t)emb;
+            float ss[1] = {0.f};
             for (int idx = tid; idx < nvec; idx += nt) {
                 float xv[VEC];
                 load_vec<T, VEC>(xv, xr + idx * VEC);
@@ -211,17 +229,28 @@ ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restr
     __shared__ float red[32];
     const int nvec = emb / VEC;
     const int tid = threadIdx.x, nt = blockDim.x;
-    for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
-        const T* xr = x + row * (int64_t)emb;
-        T* yr = y + row * (int64_t)emb;
-        float s[1] = {0.f};
-        if constexpr (NV > 0) {
+    if constexpr (NV > 0) {
+        // persistent CTAs; the next row is loaded while this one is reduced and written
+        Vec<T, VEC> xn_[NV];
+        auto load_row = [&](int64_t row) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (row < n && idx < nvec) xn_[i] = ldg_stream<T, VEC>(x + row * (int64_t)emb + idx * VEC);
+            }
+        };
+        load_row(blockIdx.x);
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            T* yr = y + row * (int64_t)emb;
             Vec<T, VEC> xc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) xc[i] = xn_[i];
+            load_row(row + gridDim.x);
+            float s[1] = {0.f};
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
                 const int idx = tid + i * nt;
                 if (idx < nvec) {
-                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) s[0] += to_f(xc[i].v[e]);
                 }
@@ -255,7 +284,12 @@ ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restr
                     store_vec<T, VEC>(yr + idx * VEC, o);
                 }
             }
-        } else {
+        }
+    } else {
+        for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+            const T* xr = x + row * (int64_t)emb;
+            T* yr = y + row * (int64_t)emb;
+            float s[1] = {0.f};
             for (int idx = tid; idx < nvec; idx += nt) {
                 float xv[VEC];
                 load_vec<T, VEC>(xv, xr + idx * VEC);
@@ -491,6 +525,18 @@ int bwd_grid(KernelT kernel, int block, int64_t n) {
     return (int)g;
 }
 
+// Forward grid: one CTA per row, except for 16-bit register-cached rows, which
+// take persistent CTAs (SM count × resident CTAs) walking rows with a one-row
+// prefetch (measured: fp32 rows move enough bytes per CTA without it).
+template <typename KernelT>
+int64_t fwd_grid(KernelT kernel, int block, int nv, int64_t n, size_t esize) {
+    if (nv == 0 || esize > 2) return rows_grid(n);
+    int occ = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, 0) != cudaSuccess || occ < 1) occ = 1;
+    const int64_t g = (int64_t)num_sms() * occ;
+    return g < n ? g : n;
+}
+
 int64_t bwd_max_parts(int64_t n) {
     int64_t g = (int64_t)num_sms() * kBwdBlocksPerSm;
     return g < n ? g : (n < 1 ? 1 : n);
@@ -520,7 +566,8 @@ int nnop_rms_norm_fwd(const void* x, const void* w, void* y, float* rstd, int64_
         RowPlan p = plan_rows<T>((int)emb, {x, w, y});
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
-                rms_fwd_kernel<T, VC, NVC><<<(unsigned)rows_grid(n), p.block, 0, s>>>(
+                auto kern = rms_fwd_kernel<T, VC, NVC>;
+                kern<<<(unsigned)fwd_grid(kern, p.block, NVC, n, sizeof(T)), p.block, 0, s>>>(
                     (const T*)x, (const T*)w, (T*)y, rstd, (int)emb, n, eps, offset, 1.0f / (float)emb);
             });
         });
@@ -576,7 +623,8 @@ int nnop_layer_norm_fwd(const void* x, const void* w, const void* b, void* y, fl
         RowPlan p = plan_rows<T>((int)emb, {x, w, b, y});
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
-                ln_fwd_kernel<T, VC, NVC><<<(unsigned)rows_grid(n), p.block, 0, s>>>(
+                auto kern = ln_fwd_kernel<T, VC, NVC>;
+                kern<<<(unsigned)fwd_grid(kern, p.block, NVC, n, sizeof(T)), p.block, 0, s>>>(
                     (const T*)x, (const T*)w, (const T*)b, (T*)y, mean, rstd, (int)emb, n, eps,
                     1.0f / (float)emb);
             });
