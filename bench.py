@@ -39,7 +39,8 @@ def cfg_flops(B, H, L, E, causal):
 
 
 # DRAM bytes (read + write) of one fa_bwd_sm100_kernel launch of config 2 at
-# B = 1, from ncu (profiles/fa_bwd_sm100_config2_b1.md).
+# B = 1, from an ncu capture of that launch (--set full, dram__bytes_read.sum +
+# dram__bytes_write.sum).
 TRAFFIC_BWD_B1 = 594.0e6
 
 
@@ -448,8 +449,8 @@ def run_ours(args):
     e2e_value = job_tflops(fwd_f + bwd_f, world, e2e_ms)
 
     hbm, tc, src = peaks()
-    # Dominant kernel: fa_bwd_sm100_kernel (largest share of the launch list,
-    # profiles/fa_config2_launches_tcgen05.md), timed live with CUDA events on
+    # Dominant kernel: fa_bwd_sm100_kernel (largest share of the ncu launch
+    # list of this workload), timed live with CUDA events on
     # its stream.  Algorithmic bytes per launch: pair tiles read and dS tiles
     # written (causal half each), q, k, v, dO read, lse and delta read, dk, dv
     # written, the fp32 dq accumulator read and written once.
@@ -460,8 +461,8 @@ def run_ours(args):
     roofline = {
         "kernel": "fa_bwd_sm100_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
         "frac": achieved / hbm, "peak_source": f"{src} hbm_gbs (burst copy)",
-        # dram__bytes_read.sum + dram__bytes_write.sum of one launch at B=1 (ncu,
-        # profiles/fa_bwd_sm100_config2_b1.md) x 8 batches: traffic grows with the batch
+        # dram__bytes_read.sum + dram__bytes_write.sum of one launch at B=1 (ncu)
+        # x the batch: traffic grows with the batch
         "traffic": TRAFFIC_BWD_B1 * B,
         "algorithmic_bytes_per_launch": kern_bytes, "launch_ms": bwd_kern_ms,
         "tensor_frac": bwd_f / (bwd_kern_ms / 1e3) / 1e12 / tc, "tensor_peak_tflops": tc,
