@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the NNop B200 hot path.
 
-Headline: flash_attention forward + backward (gradient of
+Headline workload: flash_attention forward + backward (gradient of
 sum(o) w.r.t. q, k, v and pair), bf16, E=64, L=4096, H=16, B=8 per GPU,
 causal, additive pair bias (H, QL, KL, B).  Metric: TFLOP/s with the FA2 flop
 convention 14·B·H·L²·E·½ (causal).  Weak scaling: every rank runs its own
@@ -242,7 +242,7 @@ def run_reference(args):
 
 # --------------------------------------------------------------- memory-bound ops
 def run_memory_suite(args):
-    """BASELINE config 5 (rms_norm / layer_norm on x (4096, 65536) bf16 and fp32,
+    """The memory-bound sweep (rms_norm / layer_norm on x (4096, 65536) bf16 and fp32,
     online_softmax on x (8192, 16384) fp32) and the RoPE of config 3 (q 32 heads,
     k 8 heads, L = 8192, E = 128, bf16), fwd and bwd, on one GPU: achieved HBM
     GB/s from the algorithmic bytes (each tensor read or written once) and CUDA
@@ -507,7 +507,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--suite", default="attention", choices=["attention", "memory"],
-                    help="memory: the norm / softmax / RoPE sweep (BASELINE configs 5 and 3's RoPE) on one GPU")
+                    help="memory: the norm / softmax / RoPE sweep (norm and softmax shapes, RoPE of the GQA workload) on one GPU")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override, for small profiler captures (the headline uses 8)")
     args = ap.parse_args()

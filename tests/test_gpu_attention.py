@@ -6,7 +6,7 @@ test/gqa_attention_tests.jl -- extended with bf16 and E=128, which the
 reference does not test.  Each case checks o, dq, dk, dv and dpair at two
 tolerances, both norm-based (Julia isapprox):
 * the reference's own: atol=rtol=1e-3 (fp32), 1e-1 (f16/bf16);
-* the BASELINE target: ≤1e-5 relative (fp32), ≤2e-2 relative (f16/bf16)."""
+* this implementation's parity target: ≤1e-5 relative (fp32), ≤2e-2 relative (f16/bf16)."""
 import numpy as np
 import pytest
 
@@ -134,7 +134,7 @@ def test_attention_causal_ragged_lengths():
 
 
 def test_attention_varlen_masked_tiles():
-    """Key-padding masks that blank whole key tiles (BASELINE config 4 shape,
+    """Key-padding masks that blank whole key tiles (the varlen workload's shape,
     small): pair is −Inf on padded keys like the config."""
     def mask_fn(mask, pair):
         B, KL = mask.shape
@@ -166,7 +166,7 @@ def test_attention_fully_masked_batch_gives_nan():
 
 
 def test_attention_grad_of_sum_dO_ones():
-    """The BASELINE measures ∇ sum(o) (dO = ones)."""
+    """The benchmark measures ∇ sum(o) (dO = ones)."""
     for dtype in ("bf16", "f32"):
         got, want = run_case(2, 4, 4, 512, 512, 64, dtype, False, False, False, seed=1, dO_ones=True)
         check(got, want, dtype)

@@ -5,7 +5,7 @@ dtypes and sizes the reference does not test (bf16/f16, long rows, batches).
 
 Tolerances (norm-based, Julia isapprox): the reference's own -- forward
 rtol=√eps(Float32), gradients atol=rtol=1e-6 -- for fp32; 2e-2 relative for
-bf16/f16 (the BASELINE target)."""
+bf16/f16 (the parity target of this implementation)."""
 import numpy as np
 import pytest
 
