@@ -108,3 +108,35 @@ def test_product_does_not_import_oracle():
     pkg = ROOT / "onionop.jl_b200"
     for f in pkg.rglob("*.py"):
         assert "oracle" not in f.read_text().replace("# oracle", ""), f
+
+
+def test_bwd_reuse_workspace_sizes():
+    """With the forward's pair tiles reused, the backward needs one tile buffer
+    less; without a pair, or with no (or too small) forward workspace, the
+    reuse size is the full backward size."""
+    from nnop._lib import lib
+    E, L, H, B, bf16 = 64, 4096, 16, 8, 2
+    fw = lib.nnop_flash_attention_fwd_workspace_size(E, L, L, H, H, B, 1, bf16)
+    full = lib.nnop_flash_attention_bwd_workspace_size(E, L, L, H, H, B, 1, bf16)
+    reuse = lib.nnop_flash_attention_bwd_workspace_size_reuse(E, L, L, H, H, B, 1, fw, bf16)
+    tiles = B * H * L * L * 2
+    assert fw == tiles
+    assert full - reuse == tiles
+    assert lib.nnop_flash_attention_bwd_workspace_size_reuse(E, L, L, H, H, B, 1, 0, bf16) == full
+    assert lib.nnop_flash_attention_bwd_workspace_size_reuse(E, L, L, H, H, B, 1, fw - 256, bf16) == full
+    assert (lib.nnop_flash_attention_bwd_workspace_size_reuse(E, L, L, H, H, B, 0, fw, bf16)
+            == lib.nnop_flash_attention_bwd_workspace_size(E, L, L, H, H, B, 0, bf16))
+    # fp32 and E != 64 keep no tiles
+    assert lib.nnop_flash_attention_fwd_workspace_size(E, L, L, H, H, B, 1, 0) == 0
+    assert lib.nnop_flash_attention_fwd_workspace_size(128, L, L, H, H, B, 1, bf16) == 0
+
+
+def test_kernel_timing_read_arguments():
+    from nnop._lib import lib
+    ms, n = C.c_double(1.0), C.c_int(5)
+    assert lib.nnop_kernel_timing_read(2, C.byref(ms), C.byref(n)) == -3
+    assert lib.nnop_kernel_timing_read(0, None, C.byref(n)) == -3
+    lib.nnop_kernel_timing(0)
+    # nothing recorded: zero launches, zero time (needs no device)
+    assert lib.nnop_kernel_timing_read(1, C.byref(ms), C.byref(n)) == 0
+    assert (ms.value, n.value) == (0.0, 0)
