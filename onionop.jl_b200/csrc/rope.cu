@@ -7,32 +7,19 @@
 //
 // Here the launch is out of place (the copy is fused into the rotation: read q
 // once, write q_out once).  A thread owns one 16-byte vector of the first half
-// of a (batch, position) row and its partner vector E/2 further on, loads the
-// matching cos/sin values once, and walks all max(QH, KH) heads, so the cos/sin
-// tables are read once per (batch, position) and every q/k byte moves exactly
-// once: bytes = 2·(|q| + |k|) + |cos| + |sin|.
+// of a (batch, position) row and its partner vector E/2 further on for a group
+// of kHeads heads: it loads the matching cos/sin values once, issues the loads
+// of all its heads' q and k vectors before any arithmetic, then rotates and
+// stores them.  Every q/k byte moves exactly once; the cos/sin rows are read
+// once per head group (from L2 after the first): HBM bytes =
+// 2·(|q| + |k|) + |cos| + |sin|.
 #include "common.cuh"
 
 namespace nnop {
 namespace {
 
 constexpr int kRopeBlock = 256;
-
-template <typename T, int VEC>
-__device__ __forceinline__ void rotate(const T* __restrict__ src, T* __restrict__ dst, int half,
-                                       const float (&c)[VEC], const float (&s)[VEC]) {
-    Vec<T, VEC> a = ldg_stream<T, VEC>(src);
-    Vec<T, VEC> b = ldg_stream<T, VEC>(src + half);
-    Vec<T, VEC> oa, ob;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-        const float x1 = to_f(a.v[e]), x2 = to_f(b.v[e]);
-        oa.v[e] = from_f<T>(x1 * c[e] - x2 * s[e]);
-        ob.v[e] = from_f<T>(x2 * c[e] + x1 * s[e]);
-    }
-    st_stream<T, VEC>(dst, oa);
-    st_stream<T, VEC>(dst + half, ob);
-}
+constexpr int kHeads = 4;   // heads per thread
 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kRopeBlock)
@@ -41,29 +28,58 @@ rope_kernel(const T* __restrict__ q, const T* __restrict__ k, const float* __res
             int QH, int KH, int64_t B, int64_t cos_batch, float sign) {
     const int half = E / 2;
     const int nh = half / VEC;
+    const int H = QH > KH ? QH : KH;
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t total = B * L * nh;
+    const int64_t per_group = B * L * nh;
+    const int64_t total = per_group * ((H + kHeads - 1) / kHeads);
     if (t >= total) return;
-    const int u = (int)(t % nh);
-    const int64_t l = (t / nh) % L;
-    const int64_t b = t / ((int64_t)nh * L);
+    const int hg = (int)(t / per_group);   // head group: heads hg·kHeads ..
+    const int64_t r = t % per_group;
+    const int u = (int)(r % nh);
+    const int64_t l = (r / nh) % L;
+    const int64_t b = r / ((int64_t)nh * L);
     const int64_t cb = cos_batch == 1 ? 0 : b;
     const float* cr = cos_t + (cb * L + l) * E + u * VEC;
     const float* sr = sin_t + (cb * L + l) * E + u * VEC;
-    float c[VEC], s[VEC];
+    float c[VEC], sn[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
         c[e] = __ldg(cr + e);
-        s[e] = __ldg(sr + e) * sign;
+        sn[e] = __ldg(sr + e) * sign;
     }
     const int64_t head_stride = L * E;
     const int64_t qbase = (b * QH * L + l) * E + u * VEC;
     const int64_t kbase = (b * KH * L + l) * E + u * VEC;
-    const int H = QH > KH ? QH : KH;
-#pragma unroll 4
-    for (int h = 0; h < H; ++h) {
-        if (h < QH) rotate<T, VEC>(q + qbase + h * head_stride, qo + qbase + h * head_stride, half, c, s);
-        if (h < KH) rotate<T, VEC>(k + kbase + h * head_stride, ko + kbase + h * head_stride, half, c, s);
+    // all loads of the group first
+    Vec<T, VEC> qa[kHeads], qb[kHeads], ka[kHeads], kb[kHeads];
+#pragma unroll
+    for (int j = 0; j < kHeads; ++j) {
+        const int h = hg * kHeads + j;
+        if (h < QH) {
+            qa[j] = ldg_stream<T, VEC>(q + qbase + h * head_stride);
+            qb[j] = ldg_stream<T, VEC>(q + qbase + h * head_stride + half);
+        }
+        if (h < KH) {
+            ka[j] = ldg_stream<T, VEC>(k + kbase + h * head_stride);
+            kb[j] = ldg_stream<T, VEC>(k + kbase + h * head_stride + half);
+        }
+    }
+    auto rot = [&](const Vec<T, VEC>& a, const Vec<T, VEC>& bb, T* dst) {
+        Vec<T, VEC> oa, ob;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+            const float x1 = to_f(a.v[e]), x2 = to_f(bb.v[e]);
+            oa.v[e] = from_f<T>(x1 * c[e] - x2 * sn[e]);
+            ob.v[e] = from_f<T>(x2 * c[e] + x1 * sn[e]);
+        }
+        st_stream<T, VEC>(dst, oa);
+        st_stream<T, VEC>(dst + half, ob);
+    };
+#pragma unroll
+    for (int j = 0; j < kHeads; ++j) {
+        const int h = hg * kHeads + j;
+        if (h < QH) rot(qa[j], qb[j], qo + qbase + h * head_stride);
+        if (h < KH) rot(ka[j], kb[j], ko + kbase + h * head_stride);
     }
 }
 
@@ -110,7 +126,8 @@ int nnop_llama_rope(const void* q, const void* k, const float* cos_t, const floa
         bool vec = (half % V == 0) && aligned16(cos_t) && aligned16(sin_t) &&
                    (!QH || (aligned16(q) && aligned16(q_out))) && (!KH || (aligned16(k) && aligned16(k_out)));
         const int vw = vec ? V : 1;
-        const int64_t total = B * L * (half / vw);
+        const int64_t H = QH > KH ? QH : KH;
+        const int64_t total = B * L * (half / vw) * ((H + kHeads - 1) / kHeads);
         const unsigned grid = (unsigned)((total + kRopeBlock - 1) / kRopeBlock);
         if (vec) {
             rope_kernel<T, V><<<grid, kRopeBlock, 0, s>>>((const T*)q, (const T*)k, cos_t, sin_t, (T*)q_out,
