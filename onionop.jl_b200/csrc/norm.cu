@@ -106,6 +106,69 @@ rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__
     }
 }
 
+// RMSNorm fwd, one row per CTA (no prefetch): the faster form for fp32 rows
+template <typename T, int VEC, int NV>
+__global__ void __launch_bounds__(kNormBlock)
+rms_fwd_rowwise_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+               float* __restrict__ rstd_out, int emb, int64_t n, float eps, float offset,
+               float inv_emb) {
+    __shared__ float red[32];
+    const int nvec = emb / VEC;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+        const T* xr = x + row * (int64_t)emb;
+        T* yr = y + row * (int64_t)emb;
+        float ss[1] = {0.f};
+        if constexpr (NV > 0) {
+            Vec<T, VEC> xc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        float f = to_f(xc[i].v[e]);
+                        ss[0] += f * f;
+                    }
+                }
+            }
+            block_sum<1>(ss, red);
+            const float r = 1.0f / sqrtf(ss[0] * inv_emb + eps);
+            if (tid == 0) rstd_out[row] = r;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    float wv[VEC], o[VEC];
+                    load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) o[e] = (offset + wv[e]) * to_f(xc[i].v[e]) * r;
+                    store_vec<T, VEC>(yr + idx * VEC, o);
+                }
+            }
+        } else {
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) ss[0] += xv[e] * xv[e];
+            }
+            block_sum<1>(ss, red);
+            const float r = 1.0f / sqrtf(ss[0] * inv_emb + eps);
+            if (tid == 0) rstd_out[row] = r;
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], wv[VEC], o[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(wv, w + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) o[e] = (offset + wv[e]) * xv[e] * r;
+                store_vec<T, VEC>(yr + idx * VEC, o);
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- RMSNorm bwd
 // dx = rstd·m + rstd·(−rstd²/N·dd·x), m = dy∘(w+offset), dd = Σ m∘x
 // dw partial += dy∘x·rstd      (src/rms_norm.jl:158-188)
@@ -290,6 +353,91 @@ ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restr
             const T* xr = x + row * (int64_t)emb;
             T* yr = y + row * (int64_t)emb;
             float s[1] = {0.f};
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) s[0] += xv[e];
+            }
+            block_sum<1>(s, red);
+            const float mu = s[0] * inv_emb;
+            float v[1] = {0.f};
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) { const float c = xv[e] - mu; v[0] += c * c; }
+            }
+            block_sum<1>(v, red);
+            const float r = 1.0f / sqrtf(v[0] * inv_emb + eps);
+            if (tid == 0) { mean_out[row] = mu; rstd_out[row] = r; }
+            for (int idx = tid; idx < nvec; idx += nt) {
+                float xv[VEC], wv[VEC], bv[VEC], o[VEC];
+                load_vec<T, VEC>(xv, xr + idx * VEC);
+                load_vec<T, VEC>(wv, w + idx * VEC);
+                load_vec<T, VEC>(bv, b + idx * VEC);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) o[e] = (xv[e] - mu) * r * wv[e] + bv[e];
+                store_vec<T, VEC>(yr + idx * VEC, o);
+            }
+        }
+    }
+}
+
+// LayerNorm fwd, one row per CTA (no prefetch): the faster form for fp32 rows
+template <typename T, int VEC, int NV>
+__global__ void __launch_bounds__(kNormBlock)
+ln_fwd_rowwise_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
+              T* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+              int emb, int64_t n, float eps, float inv_emb) {
+    __shared__ float red[32];
+    const int nvec = emb / VEC;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+        const T* xr = x + row * (int64_t)emb;
+        T* yr = y + row * (int64_t)emb;
+        float s[1] = {0.f};
+        if constexpr (NV > 0) {
+            Vec<T, VEC> xc[NV];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    xc[i] = ldg_stream<T, VEC>(xr + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) s[0] += to_f(xc[i].v[e]);
+                }
+            }
+            block_sum<1>(s, red);
+            const float mu = s[0] * inv_emb;
+            float v[1] = {0.f};
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        const float c = to_f(xc[i].v[e]) - mu;
+                        v[0] += c * c;
+                    }
+                }
+            }
+            block_sum<1>(v, red);
+            const float r = 1.0f / sqrtf(v[0] * inv_emb + eps);
+            if (tid == 0) { mean_out[row] = mu; rstd_out[row] = r; }
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int idx = tid + i * nt;
+                if (idx < nvec) {
+                    float wv[VEC], bv[VEC], o[VEC];
+                    load_vec<T, VEC>(wv, w + idx * VEC);
+                    load_vec<T, VEC>(bv, b + idx * VEC);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) o[e] = (to_f(xc[i].v[e]) - mu) * r * wv[e] + bv[e];
+                    store_vec<T, VEC>(yr + idx * VEC, o);
+                }
+            }
+        } else {
             for (int idx = tid; idx < nvec; idx += nt) {
                 float xv[VEC];
                 load_vec<T, VEC>(xv, xr + idx * VEC);
@@ -525,16 +673,45 @@ int bwd_grid(KernelT kernel, int block, int64_t n) {
     return (int)g;
 }
 
-// Forward grid: one CTA per row, except for 16-bit register-cached rows, which
-// take persistent CTAs (SM count × resident CTAs) walking rows with a one-row
-// prefetch (measured: fp32 rows move enough bytes per CTA without it).
+// Grid of the prefetching forward: persistent CTAs (SM count × resident CTAs)
+// walking rows with a one-row prefetch; one CTA per row without register
+// caching.  (16-bit rows only: for fp32 rows the one-row-per-CTA kernels are
+// faster, measured.)
 template <typename KernelT>
-int64_t fwd_grid(KernelT kernel, int block, int nv, int64_t n, size_t esize) {
-    if (nv == 0 || esize > 2) return rows_grid(n);
+int64_t fwd_grid(KernelT kernel, int block, int nv, int64_t n) {
+    if (nv == 0) return rows_grid(n);
     int occ = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, 0) != cudaSuccess || occ < 1) occ = 1;
     const int64_t g = (int64_t)num_sms() * occ;
     return g < n ? g : n;
+}
+
+// Forward launches: the prefetching persistent kernels for 16-bit rows, the
+// one-row-per-CTA kernels for fp32 rows (measured faster there).
+template <typename T, int VC, int NVC>
+void launch_rms_fwd(const T* x, const T* w, T* y, float* rstd, int emb, int64_t n, float eps, float offset,
+                    int block, cudaStream_t s) {
+    if constexpr (sizeof(T) <= 2) {
+        auto kern = rms_fwd_kernel<T, VC, NVC>;
+        kern<<<(unsigned)fwd_grid(kern, block, NVC, n), block, 0, s>>>(x, w, y, rstd, emb, n, eps, offset,
+                                                                        1.0f / (float)emb);
+    } else {
+        rms_fwd_rowwise_kernel<T, VC, NVC><<<(unsigned)rows_grid(n), block, 0, s>>>(x, w, y, rstd, emb, n, eps,
+                                                                                     offset, 1.0f / (float)emb);
+    }
+}
+
+template <typename T, int VC, int NVC>
+void launch_ln_fwd(const T* x, const T* w, const T* b, T* y, float* mean, float* rstd, int emb, int64_t n,
+                   float eps, int block, cudaStream_t s) {
+    if constexpr (sizeof(T) <= 2) {
+        auto kern = ln_fwd_kernel<T, VC, NVC>;
+        kern<<<(unsigned)fwd_grid(kern, block, NVC, n), block, 0, s>>>(x, w, b, y, mean, rstd, emb, n, eps,
+                                                                        1.0f / (float)emb);
+    } else {
+        ln_fwd_rowwise_kernel<T, VC, NVC><<<(unsigned)rows_grid(n), block, 0, s>>>(x, w, b, y, mean, rstd, emb, n,
+                                                                                    eps, 1.0f / (float)emb);
+    }
 }
 
 int64_t bwd_max_parts(int64_t n) {
@@ -566,9 +743,8 @@ int nnop_rms_norm_fwd(const void* x, const void* w, void* y, float* rstd, int64_
         RowPlan p = plan_rows<T>((int)emb, {x, w, y});
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
-                auto kern = rms_fwd_kernel<T, VC, NVC>;
-                kern<<<(unsigned)fwd_grid(kern, p.block, NVC, n, sizeof(T)), p.block, 0, s>>>(
-                    (const T*)x, (const T*)w, (T*)y, rstd, (int)emb, n, eps, offset, 1.0f / (float)emb);
+                launch_rms_fwd<T, VC, NVC>((const T*)x, (const T*)w, (T*)y, rstd, (int)emb, n, eps, offset,
+                                           p.block, s);
             });
         });
     });
@@ -623,10 +799,8 @@ int nnop_layer_norm_fwd(const void* x, const void* w, const void* b, void* y, fl
         RowPlan p = plan_rows<T>((int)emb, {x, w, b, y});
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
-                auto kern = ln_fwd_kernel<T, VC, NVC>;
-                kern<<<(unsigned)fwd_grid(kern, p.block, NVC, n, sizeof(T)), p.block, 0, s>>>(
-                    (const T*)x, (const T*)w, (const T*)b, (T*)y, mean, rstd, (int)emb, n, eps,
-                    1.0f / (float)emb);
+                launch_ln_fwd<T, VC, NVC>((const T*)x, (const T*)w, (const T*)b, (T*)y, mean, rstd, (int)emb, n,
+                                          eps, p.block, s);
             });
         });
     });
