@@ -140,3 +140,29 @@ def test_kernel_timing_read_arguments():
     # nothing recorded: zero launches, zero time (needs no device)
     assert lib.nnop_kernel_timing_read(1, C.byref(ms), C.byref(n)) == 0
     assert (ms.value, n.value) == (0.0, 0)
+
+
+def _bwd(lib, *, pair=None, dpair=None, ws=None, ws_bytes=0, E=64, L=256, H=2, B=1, dtype=2, align=256):
+    d = C.c_void_p(align)   # never dereferenced: validation fails first
+    return lib.nnop_flash_attention_bwd(d, d, d, d, d, d, pair, None, d, d, d, dpair, ws, ws_bytes,
+                                        E, L, L, H, H, B, 1, dtype, None)
+
+
+def test_backward_argument_errors_before_launch():
+    from nnop._lib import lib
+    d = C.c_void_p(256)
+    # dpair given exactly when pair is given
+    assert _bwd(lib, pair=d, dpair=None) == -3
+    assert _bwd(lib, pair=None, dpair=d) == -3
+    # dense tensors must be 16-byte aligned
+    assert _bwd(lib, align=8) == -6
+    # workspace missing, too small, or not 256-byte aligned
+    need = lib.nnop_flash_attention_bwd_workspace_size(64, 256, 256, 2, 2, 1, 0, 2)
+    assert need > 0
+    assert _bwd(lib, ws=None, ws_bytes=0) == -4
+    assert b"workspace too small" in lib.nnop_last_error()
+    assert _bwd(lib, ws=C.c_void_p(4096), ws_bytes=need - 1) == -4
+    assert _bwd(lib, ws=C.c_void_p(4096 + 16), ws_bytes=need) == -6
+    # the reuse variant: a forward workspace that holds no tiles changes nothing
+    full = lib.nnop_flash_attention_bwd_workspace_size_reuse(64, 256, 256, 2, 2, 1, 0, 0, 2)
+    assert full == need
