@@ -246,3 +246,43 @@ def test_norm_autograd_matches_oracle():
     assert isapprox(to_np(x.grad), dx_o, atol=0, rtol=1e-5)
     assert isapprox(to_np(w.grad), dw_o, atol=0, rtol=1e-5)
     assert isapprox(to_np(b.grad), db_o, atol=0, rtol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_norm_row_shards_sum_to_whole_job(dtype):
+    """Three ranks' row shards run on one GPU: the per-shard dx rows and the sum
+    of the per-shard dw / db are the whole job's gradients (the cross-rank sum
+    that ``allreduce_norm_grads`` performs, here summed on the host); without a
+    process group the sharded calls are the plain ones."""
+    import torch
+
+    from nnop import shards
+    nnop = _nnop()
+    rng = np.random.default_rng(12)
+    n, emb, world = 1000, 768, 3
+    x = rng.standard_normal((n, emb)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(emb)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(emb)).astype(np.float32)
+    dy = rng.standard_normal((n, emb)).astype(np.float32)
+    xd, wd, bd, dyd = (to_dev(a, dtype) for a in (x, w, b, dy))
+    xr, wr, dyr = (to_np(a) for a in (xd, wd, dyd))
+    _, rstd = nnop._rms_norm(xd, wd)
+    _, mu, rs = nnop._layer_norm(xd, wd, bd)
+    dx_rms, dx_ln, dw_rms, dw_ln, db_ln = [], [], 0.0, 0.0, 0.0
+    for r in range(world):
+        s = shards.row_shard(n, r, world)
+        dx, dw = shards.grad_rms_norm_sharded(dyd[s], rstd[s], xd[s], wd)
+        dx_rms.append(to_np(dx))
+        dw_rms = dw_rms + to_np(dw)
+        dx, dw, db = shards.grad_layer_norm_sharded(dyd[s], mu[s], rs[s], xd[s], wd)
+        dx_ln.append(to_np(dx))
+        dw_ln, db_ln = dw_ln + to_np(dw), db_ln + to_np(db)
+    tol = dict(atol=0, rtol=1e-5) if dtype == "f32" else dict(atol=0, rtol=TOL_HALF)
+    dx_o, dw_o = orc.rms_norm_bwd(dyr, xr, wr)
+    assert isapprox(np.concatenate(dx_rms), dx_o, **tol) and isapprox(dw_rms, dw_o, **tol)
+    dx_o, dw_o, db_o = orc.layer_norm_bwd(dyr, xr, wr)
+    assert isapprox(np.concatenate(dx_ln), dx_o, **tol)
+    assert isapprox(dw_ln, dw_o, **tol) and isapprox(db_ln, db_o, **tol)
+    whole = nnop.grad_rms_norm(dyd, rstd, xd, wd)
+    one = shards.grad_rms_norm_sharded(dyd, rstd, xd, wd)
+    assert all(torch.equal(a, c) for a, c in zip(whole, one))

@@ -63,3 +63,57 @@ def test_two_gloo_ranks(tmp_path):
         seeds.add(int(row[7]))
         assert int(row[8]) == 0   # rank 1's reference arm printed nothing
     assert len(seeds) == 2       # each rank its own batch shard
+
+
+def _norm_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), LOCAL_RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    sys.path[:0] = [str(ROOT), str(ROOT / "onionop.jl_b200")]
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from nnop import shards
+    from oracle import nnop_oracle as orc
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        rng = np.random.default_rng(11)            # the same full job on every rank
+        n, emb = 37, 24                            # 37 rows: shards of 19 and 18
+        x, dy = rng.standard_normal((n, emb)), rng.standard_normal((n, emb))
+        w = 1 + 0.1 * rng.standard_normal(emb)
+        rows = shards.row_shard(n, rank, world)
+        _, dw_rms = orc.rms_norm_bwd(dy[rows], x[rows], w)
+        _, dw_ln, db_ln = orc.layer_norm_bwd(dy[rows], x[rows], w)
+        (dw_rms_t,) = shards.allreduce_norm_grads(torch.from_numpy(dw_rms).float())
+        dw_ln_t, db_ln_t = shards.allreduce_norm_grads(torch.from_numpy(dw_ln).bfloat16(),
+                                                       torch.from_numpy(db_ln).bfloat16())
+        assert dw_ln_t.dtype == torch.bfloat16 and db_ln_t.shape == (emb,)
+        np.savez(pathlib.Path(out_dir) / f"norm{rank}.npz", rows=np.array([rows.start, rows.stop]),
+                 dw_rms=dw_rms_t.double().numpy(), dw_ln=dw_ln_t.double().numpy(), db_ln=db_ln_t.double().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_norm_grads(tmp_path):
+    import numpy as np
+    import torch.multiprocessing as mp
+
+    from oracle import nnop_oracle as orc
+    port = _free_port()
+    mp.start_processes(_norm_worker, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    got = [np.load(tmp_path / f"norm{r}.npz") for r in range(2)]
+    assert [tuple(g["rows"]) for g in got] == [(0, 19), (19, 37)]
+    rng = np.random.default_rng(11)
+    n, emb = 37, 24
+    x, dy = rng.standard_normal((n, emb)), rng.standard_normal((n, emb))
+    w = 1 + 0.1 * rng.standard_normal(emb)
+    _, dw_rms = orc.rms_norm_bwd(dy, x, w)
+    _, dw_ln, db_ln = orc.layer_norm_bwd(dy, x, w)
+    for g in got:                                  # every rank holds the whole job's gradients
+        np.testing.assert_allclose(g["dw_rms"], dw_rms, rtol=1e-5, atol=1e-5)
+        # 16-bit partials: each rank's value rounded once, the sum rounded once
+        np.testing.assert_allclose(g["dw_ln"], dw_ln, rtol=2e-2, atol=5e-2)
+        np.testing.assert_allclose(g["db_ln"], db_ln, rtol=2e-2, atol=5e-2)
+    assert all((got[0][k] == got[1][k]).all() for k in ("dw_rms", "dw_ln", "db_ln"))
