@@ -184,7 +184,7 @@ class CpuAttention:
     def __init__(self, batches: int = 1):
         import numpy as np
 
-        from oracle import cpu_attention as ca
+        from oracle import cpu_oracle as ca
         from oracle import nnop_oracle as orc
         self.ca = ca
         E, L, H = CFG["E"], CFG["L"], CFG["H"]
@@ -255,6 +255,61 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------- memory-bound ops
+def cpu_memory_rows(reps: int = 3) -> dict:
+    """The memory suite's ops on the host cores: the fp32 C restatement
+    (oracle/cpu/memops_cpu.c, every core of the CPU set) on the same shapes
+    (norms x (65536 rows, 4096); softmax x (16384 rows, 8192); the RoPE of the
+    GQA workload), one untimed call then the mean of `reps` calls, outputs
+    reused.  GB/s from the fp32 algorithmic bytes (each tensor read or written
+    once)."""
+    import numpy as np
+
+    from oracle import cpu_oracle as ca
+    rng = np.random.default_rng(5)
+    res = {}
+
+    def timed(name, nbytes, fn):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        ms = (time.perf_counter() - t0) / reps * 1e3
+        res[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9}
+
+    n, emb = 65536, 4096
+    x = rng.standard_normal((n, emb), dtype=np.float32)
+    dy = rng.standard_normal((n, emb), dtype=np.float32)
+    w = (1 + 0.1 * rng.standard_normal(emb)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(emb)).astype(np.float32)
+    big, rows_, vec = np.empty_like(x), np.empty(n, np.float32), np.empty(emb, np.float32)
+    _, rstd = ca.rms_norm_fwd(x, w)
+    timed("rms_norm_fwd_f32", 2 * x.nbytes, lambda: ca.rms_norm_fwd(x, w, out=(big, rows_)))
+    timed("rms_norm_bwd_f32", 3 * x.nbytes, lambda: ca.rms_norm_bwd(dy, rstd, x, w, out=(big, vec)))
+    _, mu, rs = ca.layer_norm_fwd(x, w, b)
+    rows2 = np.empty(n, np.float32)
+    timed("layer_norm_fwd_f32", 2 * x.nbytes, lambda: ca.layer_norm_fwd(x, w, b, out=(big, rows_, rows2)))
+    timed("layer_norm_bwd_f32", 3 * x.nbytes,
+          lambda: ca.layer_norm_bwd(dy, mu, rs, x, w, out=(big, vec, np.empty(emb, np.float32))))
+    del x, dy, big
+    x = (2 * rng.standard_normal((16384, 8192), dtype=np.float32))
+    y, dx = ca.softmax_fwd(x), np.empty_like(x)
+    dy = rng.standard_normal(x.shape, dtype=np.float32)
+    timed("online_softmax_fwd_f32", 2 * x.nbytes, lambda: ca.softmax_fwd(x, out=dx))
+    timed("online_softmax_bwd_f32", 3 * x.nbytes, lambda: ca.softmax_bwd(dy, y, out=dx))
+    del x, y, dx, dy
+    B, QH, KH, L, E = 4, 32, 8, 8192, 128
+    q = rng.standard_normal((B, QH, L, E), dtype=np.float32)
+    k = rng.standard_normal((B, KH, L, E), dtype=np.float32)
+    from oracle import nnop_oracle as orc
+    cos, sin = orc.llama_rotary_embedding(E, np.tile(np.arange(L, dtype=np.float32), (B, 1)))
+    qo, ko = np.empty_like(q), np.empty_like(k)
+    rb = 2 * (q.nbytes + k.nbytes) + cos.nbytes + sin.nbytes
+    timed("llama_rope_fwd_f32", rb, lambda: ca.llama_rope(q, k, cos, sin, out=(qo, ko)))
+    timed("llama_rope_bwd_f32", rb, lambda: ca.llama_rope(q, k, cos, sin, sign=-1.0, out=(qo, ko)))
+    return {"ops": res, "cores": ca.host_threads(), "kind": "port", "dtype": "f32",
+            "sample": f"C restatement (oracle/cpu/memops_cpu.c), fp32, full shapes, mean of {reps} calls"}
+
+
 def run_memory_suite(args):
     """The memory-bound sweep (rms_norm / layer_norm on x (4096, 65536) bf16 and fp32,
     online_softmax on x (8192, 16384) fp32) and the RoPE of config 3 (q 32 heads,
@@ -319,8 +374,11 @@ def run_memory_suite(args):
     rb = 2 * (q.numel() + k.numel()) * 2 + 2 * cos.numel() * 4
     add("llama_rope_fwd_bf16", rb, timed(lambda: nnop.llama_rope(q, k, cos=cos, sin=sin)))
     add("llama_rope_bwd_bf16", rb, timed(lambda: nnop.grad_llama_rope(q, k, cos=cos, sin=sin)))
+    del q, k, cos, sin
+    torch.cuda.empty_cache()
     out = {"suite": "memory", "unit": "GB/s", "peak": hbm, "peak_source": f"{src} hbm_gbs", "steps": K,
            "warmup": W, "ops": rows,
+           "cpu_baseline": None if args.no_cpu else cpu_memory_rows(),
            "config": {"norms": "x (4096, 65536) Julia = [65536][4096] rows, w (and b) (4096,)",
                       "softmax": "x (8192, 16384) fp32, dim 1", "rope": "q (128, 8192, 32, 4), k (128, 8192, 8, 4) bf16"}}
     print(json.dumps(out), flush=True)
@@ -485,7 +543,7 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tf, n, dt_s, text = cpu_attention_sample(seconds=args.cpu_seconds)
-        from oracle import cpu_attention as ca
+        from oracle import cpu_oracle as ca
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": ca.host_threads(), "kind": "port",
                "sample": f"{text}, {dt_s:.1f} s"}
     if rank == 0:

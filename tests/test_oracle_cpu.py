@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 from _util import isapprox
-from oracle import cpu_attention as ca
+from oracle import cpu_oracle as ca
 from oracle import nnop_oracle as orc
 
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "oracle_golden.npz"
@@ -137,3 +137,59 @@ def test_output_reuse_and_errors():
         ca.attention_fwd(q[..., :24], k[..., :24], v[..., :24], None, scale=0.2)
     with pytest.raises(ValueError):                                  # QH must be a multiple of KH
         ca.attention_fwd(q, np.concatenate([k, k, k], 1), np.concatenate([v, v, v], 1), None, scale=0.2)
+
+
+# ------------------------------------------------------------ memory-bound ops
+@pytest.mark.parametrize("emb,n", [(4096, 33), (513, 25), (15, 7), (1024, 1)])
+@pytest.mark.parametrize("threads", [1, 4])
+def test_norms_against_float64_oracle(emb, n, threads):
+    rng = np.random.default_rng(emb + n)
+    x = rng.standard_normal((n, emb)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(emb)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(emb)).astype(np.float32)
+    dy = rng.standard_normal((n, emb)).astype(np.float32)
+    for offset in (0.0, 1.0):
+        y, rstd = ca.rms_norm_fwd(x, w, offset=offset, threads=threads)
+        yo, ro = orc.rms_norm_fwd(x, w, offset=offset)
+        assert isapprox(y, yo, **TOL) and isapprox(rstd, ro, **TOL)
+        dx, dw = ca.rms_norm_bwd(dy, rstd, x, w, offset=offset, threads=threads)
+        dxo, dwo = orc.rms_norm_bwd(dy, x, w, offset=offset)
+        assert isapprox(dx, dxo, **TOL) and isapprox(dw, dwo, **TOL)
+    y, mu, rs = ca.layer_norm_fwd(x, w, b, threads=threads)
+    yo, muo, rso = orc.layer_norm_fwd(x, w, b)
+    assert isapprox(y, yo, **TOL) and isapprox(mu, muo, atol=1e-6, rtol=1e-5) and isapprox(rs, rso, **TOL)
+    got = ca.layer_norm_bwd(dy, mu, rs, x, w, threads=threads)
+    for a, o in zip(got, orc.layer_norm_bwd(dy, x, w)):
+        assert isapprox(a, o, **TOL)
+
+
+@pytest.mark.parametrize("rows,N", [(7, 9), (33, 1000), (1, 4), (5, 8193)])
+def test_softmax_against_float64_oracle(rows, N):
+    rng = np.random.default_rng(rows * N)
+    x = (4 * rng.standard_normal((rows, N))).astype(np.float32)
+    x[0, ::3] = -np.inf
+    dy = rng.standard_normal((rows, N)).astype(np.float32)
+    y = ca.softmax_fwd(x, threads=3)
+    assert isapprox(y, orc.softmax_fwd(x), **TOL) and not y[0, ::3].any()
+    # gradient: the reference tests' absolute floor (1e-6) covers rows whose
+    # dx cancels to far below dy (a row with one dominant probability)
+    assert isapprox(ca.softmax_bwd(dy, y, threads=3), orc.softmax_bwd(dy, y), atol=1e-6, rtol=1e-5)
+    if rows > 1:
+        x[1] = -np.inf                                 # an all -Inf row: NaN like the naive softmax
+        assert np.isnan(ca.softmax_fwd(x)[1]).all() and np.isnan(orc.softmax_fwd(x)[1]).all()
+
+
+@pytest.mark.parametrize("E,L,QH,KH,B", [(128, 300, 8, 2, 3), (64, 1025, 3, 5, 2), (16, 7, 1, 1, 1)])
+def test_rope_against_float64_oracle(E, L, QH, KH, B):
+    rng = np.random.default_rng(E + L)
+    q = rng.standard_normal((B, QH, L, E)).astype(np.float32)
+    k = rng.standard_normal((B, KH, L, E)).astype(np.float32)
+    pos = np.tile(np.arange(L, dtype=np.float32), (B, 1))
+    cos, sin = orc.llama_rotary_embedding(E, pos)
+    for sign, fn in ((1.0, orc.rope_fwd), (-1.0, orc.rope_bwd)):
+        qo, ko = ca.llama_rope(q, k, cos, sin, sign=sign, threads=4)
+        qw, kw = fn(q, k, cos, sin)
+        assert isapprox(qo, qw, **TOL) and isapprox(ko, kw, **TOL)
+    ones = np.ones((1, 1, L, E), np.float32)             # the reference's q = k = ones case
+    qo, _ = ca.llama_rope(ones, ones, cos[:1], sin[:1])
+    assert isapprox(qo, orc.rope_fwd(ones, ones, cos[:1], sin[:1])[0], **TOL)
