@@ -384,6 +384,108 @@ def run_memory_suite(args):
     print(json.dumps(out), flush=True)
 
 
+# --------------------------------------------------------------- other attention configs
+def run_configs_suite(args):
+    """The attention configurations beside the headline one, fwd + bwd through
+    the public API on one GPU (CUDA events over K steps after W warm-ups):
+      1  fp32 E=64 L=512 H=4 B=2, non-causal, no bias, q,k,v ~ U[0,1), dO = ones;
+      3  bf16 GQA E=128 L=8192 QH=32 KH=8 B=4, causal: RoPE (positions 0..L-1,
+         base 10000) on q and k, attention fwd + bwd, RoPE bwd;
+      4  fp16 E=64 H=8 B=16 L=4096, key lengths ~ U{256..4096} (seed 4) behind
+         a key-padding mask, pair ~ N(0, 0.5) with -Inf at masked keys,
+         non-causal -- TFLOP/s both on the effective flops (masked key tiles
+         skipped: 14 H E L sum(len_b)) and on the padded ones (14 B H L^2 E).
+    FA2 flop convention; inputs of configs 3 and 4 are larger than L2."""
+    import numpy as np
+    import torch
+
+    import nnop
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _, tc, src = peaks()
+    K, W = max(args.steps, 3), max(args.warmup, 3)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / K
+
+    rows = {}
+    # config 1
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    B, H, L, E = 2, 4, 512, 64
+    q, k, v = (torch.rand(B, H, L, E, device=dev, generator=g) for _ in range(3))
+    do = torch.ones(B, H, L, E, device=dev)
+
+    def step1():
+        o, lse = nnop._flash_attention(q, k, v, causal=False)
+        nnop.grad_flash_attention(do, o, lse, q, k, v, causal=False)
+    ms = timed(step1)
+    f = sum(cfg_flops(B, H, L, E, False))
+    rows["config1_fp32"] = {"ms": ms, "TFLOP/s": f / (ms / 1e3) / 1e12, "flops": f}
+    del q, k, v, do
+    # config 3
+    g.manual_seed(3)
+    B, QH, KH, L, E = 4, 32, 8, 8192, 128
+    q = torch.randn(B, QH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    do = torch.ones(B, QH, L, E, device=dev, dtype=torch.bfloat16)
+    pos = torch.arange(L, device=dev, dtype=torch.float32).repeat(B, 1)
+    cos, sin = nnop.LlamaRotaryEmbedding(E)(pos)
+
+    def attn3(qr, kr):
+        o, lse = nnop._flash_attention(qr, kr, v, causal=True)
+        return nnop.grad_flash_attention(do, o, lse, qr, kr, v, causal=True)
+
+    def step3():
+        qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
+        dq, dk, _, _ = attn3(qr, kr)
+        nnop.grad_llama_rope(dq, dk, cos=cos, sin=sin)
+    qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
+    ms_attn = timed(lambda: attn3(qr, kr))
+    ms = timed(step3)
+    f = 14.0 * B * QH * L * L * E * 0.5
+    rows["config3_gqa_rope_bf16"] = {"ms": ms, "attention_ms": ms_attn, "TFLOP/s": f / (ms / 1e3) / 1e12,
+                                      "attention_TFLOP/s": f / (ms_attn / 1e3) / 1e12,
+                                      "tensor_frac": f / (ms_attn / 1e3) / 1e12 / tc, "flops": f}
+    del q, k, v, do, qr, kr, cos, sin, pos
+    torch.cuda.empty_cache()
+    # config 4
+    B, H, L, E = 16, 8, 4096, 64
+    lens = np.random.default_rng(4).integers(256, L + 1, size=B)
+    g.manual_seed(4)
+    q, k, v = (torch.randn(B, H, L, E, device=dev, dtype=torch.float16, generator=g) for _ in range(3))
+    do = torch.ones(B, H, L, E, device=dev, dtype=torch.float16)
+    pair = (0.5 * torch.randn(B, L, L, H, device=dev, generator=g)).to(torch.float16)
+    mask = torch.zeros(B, L, dtype=torch.bool, device=dev)
+    for b, n in enumerate(lens):
+        mask[b, :n] = True
+        pair[b, n:] = -float("inf")
+
+    def step4():
+        o, lse, ws = nnop._flash_attention_ws(q, k, v, pair, causal=False, kpad_mask=mask)
+        nnop.grad_flash_attention(do, o, lse, q, k, v, pair, causal=False, kpad_mask=mask, fwd_workspace=ws)
+    ms = timed(step4)
+    f_eff = 14.0 * H * E * L * float(lens.sum())
+    f_pad = 14.0 * B * H * L * L * E
+    rows["config4_varlen_pair_f16"] = {"ms": ms, "TFLOP/s_effective": f_eff / (ms / 1e3) / 1e12,
+                                       "TFLOP/s_padded": f_pad / (ms / 1e3) / 1e12, "flops_effective": f_eff,
+                                       "flops_padded": f_pad, "sum_len": int(lens.sum())}
+    out = {"suite": "configs", "unit": "TFLOP/s", "tensor_peak_tflops": tc, "peak_source": f"{src} bf16_tflops",
+           "steps": K, "warmup": W, "configs": rows, "data": "synthetic, seeded by config index"}
+    print(json.dumps(out), flush=True)
+
+
 # --------------------------------------------------------------- GPU arm
 def run_ours(args):
     import torch
@@ -578,8 +680,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--suite", default="attention", choices=["attention", "memory"],
-                    help="memory: the norm / softmax / RoPE sweep (norm and softmax shapes, RoPE of the GQA workload) on one GPU")
+    ap.add_argument("--suite", default="attention", choices=["attention", "memory", "configs"],
+                    help="memory: the norm / softmax / RoPE sweep (norm and softmax shapes, RoPE of the GQA workload) "
+                         "on one GPU; configs: the fp32, GQA+RoPE and variable-length attention configurations")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override, for small profiler captures (the headline uses 8)")
     args = ap.parse_args()
@@ -589,6 +692,8 @@ def main():
         run_reference(args)
     elif args.suite == "memory":
         run_memory_suite(args)
+    elif args.suite == "configs":
+        run_configs_suite(args)
     else:
         run_ours(args)
 
