@@ -453,11 +453,17 @@ def run_configs_suite(args):
         nnop.grad_llama_rope(dq, dk, cos=cos, sin=sin)
     qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
     ms_attn = timed(lambda: attn3(qr, kr))
+    ms_fwd = timed(lambda: nnop._flash_attention(qr, kr, v, causal=True))
+    o3, lse3 = nnop._flash_attention(qr, kr, v, causal=True)
+    ms_bwd = timed(lambda: nnop.grad_flash_attention(do, o3, lse3, qr, kr, v, causal=True))
     ms = timed(step3)
     f = 14.0 * B * QH * L * L * E * 0.5
     rows["config3_gqa_rope_bf16"] = {"ms": ms, "attention_ms": ms_attn, "TFLOP/s": f / (ms / 1e3) / 1e12,
                                       "attention_TFLOP/s": f / (ms_attn / 1e3) / 1e12,
-                                      "tensor_frac": f / (ms_attn / 1e3) / 1e12 / tc, "flops": f}
+                                      "tensor_frac": f / (ms_attn / 1e3) / 1e12 / tc, "flops": f,
+                                      "fwd_ms": ms_fwd, "fwd_TFLOP/s": f / 3.5 / (ms_fwd / 1e3) / 1e12,
+                                      "bwd_ms": ms_bwd, "bwd_TFLOP/s": f / 3.5 * 2.5 / (ms_bwd / 1e3) / 1e12}
+    del o3, lse3
     del q, k, v, do, qr, kr, cos, sin, pos
     torch.cuda.empty_cache()
     # config 4
