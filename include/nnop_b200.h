@@ -88,8 +88,8 @@ int nnop_kernel_timing_read(int which, double* total_ms, int* count);
  * -------------------------------------------------------------------------- */
 
 /*
- * Forward.  Replaces `_flash_attention` (src/attention.jl:177-229) and its
- * kernel `_flash_attention_fwd!` (src/attention.jl:40-175).
+ * Forward.  Replaces `_flash_attention` (src/attention.jl:145-197) and its
+ * kernel `_flash_attention_fwd!` (src/attention.jl:8-143).
  *
  *   q    [B][QH][QL][E]    (Julia q  (E, QL, QH, B))
  *   k, v [B][KH][KL][E]    (Julia k, v (E, KL, KH, B)); k and v share a shape
@@ -102,7 +102,7 @@ int nnop_kernel_timing_read(int which, double* total_ms, int* count);
  *
  * logits s_ij = scale·(q_i·k_j) [+ pair] with key j masked (−Inf) when
  * causal && j > i or kpad_mask[b][j] == 0; scale = dtype(1/sqrt(E)).
- * Checks (src/attention.jl:185-188): E must be a power of two (16..128 here),
+ * Checks (src/attention.jl:153-156): E must be a power of two (16..128 here),
  * QH % KH == 0.  dtype: F32, F16, BF16.
  *   workspace: with a pair bias, >= nnop_flash_attention_fwd_workspace_size(...)
  *   bytes, 256-byte aligned, holding per-head copies of the pair tiles for the
@@ -204,8 +204,8 @@ int nnop_online_softmax_bwd(const void* dy, const void* y, void* dx,
  * -------------------------------------------------------------------------- */
 
 /*
- * Forward.  Replaces `_rms_norm` (src/rms_norm.jl:203-223) and `_rms_norm!`
- * (src/rms_norm.jl:89-124).
+ * Forward.  Replaces `_rms_norm` (src/rms_norm.jl:117-137) and `_rms_norm!`
+ * (src/rms_norm.jl:3-38).
  *   x, y [n][emb] dtype; w [emb] dtype; rstd [n] f32 = 1/sqrt(mean(x²)+eps)
  *   y = (offset + w)·x·rstd
  */
@@ -216,8 +216,8 @@ int nnop_rms_norm_fwd(const void* x, const void* w, void* y, float* rstd,
 size_t nnop_rms_norm_bwd_workspace_size(int64_t emb, int64_t n);
 
 /*
- * Backward.  Replaces `∇rms_norm` (src/rms_norm.jl:225-255) and `_∇rms_norm!`
- * (src/rms_norm.jl:129-201).
+ * Backward.  Replaces `∇rms_norm` (src/rms_norm.jl:139-169) and `_∇rms_norm!`
+ * (src/rms_norm.jl:43-115).
  *   dy, x, dx [n][emb] dtype; w [emb] dtype; rstd [n] f32 (from the forward);
  *   dw [emb] f32 (the reference returns a Float32 dw as well).
  */
@@ -281,7 +281,7 @@ int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w,
 
 /*
  * Rotation of q and k in one launch.  Replaces `_llama_rope`
- * (src/rope/llama_rope.jl:289-309) and `llama_rope!` (:244-285).
+ * (src/rope/llama_rope.jl:69-89) and `llama_rope!` (:24-65).
  *   q, q_out [B][QH][L][E]; k, k_out [B][KH][L][E] (dtype)
  *   cos, sin [cos_batch][L][E] f32 (Julia (E, L, batch)); cos_batch is B, or
  *   1 to share one table across the batch.
@@ -297,7 +297,7 @@ int nnop_llama_rope(const void* q, const void* k,
 
 /*
  * cos/sin tables of `LlamaRotaryEmbedding(dim; base)(position_ids)`
- * (src/rope/llama_rope.jl:227-242) computed on the device.
+ * (src/rope/llama_rope.jl:7-22) computed on the device.
  *   position_ids [B][L] f32 (Julia (L, B)); cos_t, sin_t [B][L][dim] f32.
  */
 int nnop_llama_rope_cos_sin(const float* position_ids, float* cos_t, float* sin_t,

@@ -1,5 +1,5 @@
 // C-ABI entry points of flash attention: argument checks (the reference's
-// `_flash_attention` / `∇flash_attention` error()s, src/attention.jl:185-188 and
+// `_flash_attention` / `∇flash_attention` error()s, src/attention.jl:153-156 and
 // src/attention_bwd.jl:224-227), workspace layout and kernel dispatch.
 #include "fa_common.cuh"
 

@@ -1,7 +1,7 @@
 // Flash-attention forward on the sm_100a tensor cores (tcgen05 UMMA, TMEM
 // accumulators, TMA-fed tiles), bf16/f16, E in {64, 128}.
 //
-// Reference: `_flash_attention_fwd!` (src/attention.jl:40-175) -- one thread
+// Reference: `_flash_attention_fwd!` (src/attention.jl:8-143) -- one thread
 // per query row with the scores in shared memory and WMMA 16x16x16 tiles.
 //
 // One CTA per (128-query tile, query head, batch); 256 threads:

@@ -2,7 +2,7 @@
 // (mma.sync m16n8k16, fp32 accumulation).  This is the general path: every E
 // in {16, 32, 64, 128}, pair bias, causal, GQA and key padding.
 //
-// Reference: `_flash_attention_fwd!` (src/attention.jl:40-175) and
+// Reference: `_flash_attention_fwd!` (src/attention.jl:8-143) and
 // `_flash_attention_bwd!` (src/attention_bwd.jl:1-175).  The reference's forward
 // keeps the softmax state in shared memory with one thread per query row and
 // WMMA 16x16x16 tiles; its backward runs one workgroup per (head, batch) over

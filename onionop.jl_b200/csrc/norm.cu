@@ -1,6 +1,6 @@
 // RMSNorm and LayerNorm, forward and backward, for sm_100a.
 //
-// Reference: src/rms_norm.jl (kernels :89-201, launchers :203-255) and
+// Reference: src/rms_norm.jl (kernels :3-115, launchers :117-169) and
 // src/layer_norm.jl (kernels :8-148, launchers :150-204).
 //
 // Design (HBM-bound, 2·N·s bytes forward, 3·N·s backward):
@@ -14,7 +14,7 @@
 //   owns the same columns for every row it visits, so dw/db accumulate in
 //   registers, and each CTA writes one fp32 partial row to the workspace.  A
 //   second, deterministic kernel sums the partials over CTAs (the reference
-//   sums a (n/4, emb) partial with `sum(dw; dims=1)`, src/rms_norm.jl:248-253).
+//   sums a (n/4, emb) partial with `sum(dw; dims=1)`, src/rms_norm.jl:162-167).
 // * rows whose length is not a multiple of the 16-byte vector, or unaligned
 //   base pointers, take the same kernels with a vector width of one element.
 #include "common.cuh"
@@ -171,7 +171,7 @@ rms_fwd_rowwise_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __re
 
 // ---------------------------------------------------------------- RMSNorm bwd
 // dx = rstd·m + rstd·(−rstd²/N·dd·x), m = dy∘(w+offset), dd = Σ m∘x
-// dw partial += dy∘x·rstd      (src/rms_norm.jl:158-188)
+// dw partial += dy∘x·rstd      (src/rms_norm.jl:97-101)
 template <typename T, int VEC, int NV>
 __global__ void __launch_bounds__(kNormBlock)
 rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,

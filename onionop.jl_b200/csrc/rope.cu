@@ -1,9 +1,9 @@
 // Llama RoPE (q and k in one launch) and the LlamaRotaryEmbedding cos/sin
 // tables, for sm_100a.
 //
-// Reference: src/rope/llama_rope.jl -- `llama_rope!` (:244-285) gives each
+// Reference: src/rope/llama_rope.jl -- `llama_rope!` (:24-65) gives each
 // thread one sequence position of one head and walks E/2 element pairs with a
-// thread stride of E (uncoalesced), on copies of q and k made first (:295-296).
+// thread stride of E (uncoalesced), on copies of q and k made first (:75-76).
 //
 // Here the launch is out of place (the copy is fused into the rotation: read q
 // once, write q_out once).  A thread owns one 16-byte vector of the first half
@@ -84,7 +84,7 @@ rope_kernel(const T* __restrict__ q, const T* __restrict__ k, const float* __res
 }
 
 // cos/sin of inv_freq[i mod dim/2] · position, inv_freq[i] = 1/base^(2i/dim),
-// in float32 like `LlamaRotaryEmbedding` (src/rope/llama_rope.jl:227-242).
+// in float32 like `LlamaRotaryEmbedding` (src/rope/llama_rope.jl:7-22).
 __global__ void rope_table_kernel(const float* __restrict__ pos, float* __restrict__ cos_t,
                                   float* __restrict__ sin_t, int dim, int64_t L, int64_t B, float base) {
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

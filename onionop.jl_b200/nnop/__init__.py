@@ -111,7 +111,7 @@ def _fa_dims(q, k, v, pair, kpad_mask):
 
 
 def _flash_attention(q, k, v, pair=None, *, causal: bool, kpad_mask=None):
-    """Forward returning ``(o, lse)`` (``_flash_attention``, src/attention.jl:177-229,
+    """Forward returning ``(o, lse)`` (``_flash_attention``, src/attention.jl:145-197,
     which returns ``(o, ms, ls)``; here ``lse = ms + log(ls)`` in float32)."""
     o, lse, _ = _flash_attention_ws(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)
     return o, lse
@@ -250,7 +250,7 @@ def _norm_dims(x, w):
 
 
 def _rms_norm(x, w, *, eps: float = 1e-6, offset: float = 0.0):
-    """``_rms_norm`` (src/rms_norm.jl:203-223): returns ``(y, rstd)``."""
+    """``_rms_norm`` (src/rms_norm.jl:117-137): returns ``(y, rstd)``."""
     dev = _dev(x, w)
     x = x.contiguous()
     w = w.contiguous().to(x.dtype)
@@ -263,7 +263,7 @@ def _rms_norm(x, w, *, eps: float = 1e-6, offset: float = 0.0):
 
 
 def grad_rms_norm(dy, rstd, x, w, *, offset: float = 0.0):
-    """``∇rms_norm`` (src/rms_norm.jl:225-255): returns ``(dx, dw)``, dw float32."""
+    """``∇rms_norm`` (src/rms_norm.jl:139-169): returns ``(dx, dw)``, dw float32."""
     dev = _dev(dy, rstd, x, w)
     x = x.contiguous()
     w = w.contiguous().to(x.dtype)
@@ -279,7 +279,7 @@ def grad_rms_norm(dy, rstd, x, w, *, offset: float = 0.0):
 
 
 class _RmsNormFn(torch.autograd.Function):
-    """``CRC.rrule(::typeof(_rms_norm), x, w)`` (src/rms_norm.jl:264-271)."""
+    """``CRC.rrule(::typeof(_rms_norm), x, w)`` (src/rms_norm.jl:178-185)."""
 
     @staticmethod
     def forward(ctx, x, w, eps, offset):
@@ -296,7 +296,7 @@ class _RmsNormFn(torch.autograd.Function):
 
 
 def rms_norm(x, w, *, eps: float = 1e-6, offset: float = 0.0):
-    """``NNop.rms_norm(x, w; ϵ=1f-6, offset=0f0)`` (src/rms_norm.jl:257-262)."""
+    """``NNop.rms_norm(x, w; ϵ=1f-6, offset=0f0)`` (src/rms_norm.jl:171-176)."""
     if within_gradient(x) or within_gradient(w):
         return _RmsNormFn.apply(x, w, float(eps), float(offset))
     return _rms_norm(x, w, eps=eps, offset=offset)[0]
@@ -370,7 +370,7 @@ def layer_norm(x, w, b, *, eps: float = 1e-6):
 # =========================================================================
 
 class LlamaRotaryEmbedding:
-    """``LlamaRotaryEmbedding(dim; base=10000)`` (src/rope/llama_rope.jl:221-242).
+    """``LlamaRotaryEmbedding(dim; base=10000)`` (src/rope/llama_rope.jl:1-22).
 
     ``emb(position_ids)`` with position_ids (B, L) float32 returns ``(cos, sin)``
     of shape (B, L, dim) float32, computed on the device."""
@@ -420,12 +420,12 @@ def _llama_rope(q, k, cos, sin, *, bwd: bool):
 
 
 def grad_llama_rope(dq, dk, *, cos, sin):
-    """``∇llama_rope`` (src/rope/llama_rope.jl:312): the rotation with sin → −sin."""
+    """``∇llama_rope`` (src/rope/llama_rope.jl:92): the rotation with sin → −sin."""
     return _llama_rope(dq, dk, cos, sin, bwd=True)
 
 
 class _RopeFn(torch.autograd.Function):
-    """``CRC.rrule(::typeof(llama_rope), q, k; cos, sin)`` (src/rope/llama_rope.jl:314-318)."""
+    """``CRC.rrule(::typeof(llama_rope), q, k; cos, sin)`` (src/rope/llama_rope.jl:94-98)."""
 
     @staticmethod
     def forward(ctx, q, k, cos, sin):
@@ -442,7 +442,7 @@ class _RopeFn(torch.autograd.Function):
 
 
 def llama_rope(q, k, *, cos, sin):
-    """``NNop.llama_rope(q, k; cos, sin)`` (src/rope/llama_rope.jl:311): returns
+    """``NNop.llama_rope(q, k; cos, sin)`` (src/rope/llama_rope.jl:91): returns
     rotated copies ``(q, k)``."""
     if within_gradient(q) or within_gradient(k):
         return _RopeFn.apply(q, k, cos, sin)

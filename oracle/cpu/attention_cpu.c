@@ -8,7 +8,7 @@
  * What it restates (reference package NNop v0.2.0, Julia):
  *   forward   src/attention.jl:8-143  -- blocks of queries against blocks of
  *             keys, logits (q.k)*scale + pair, causal mask "key j visible to
- *             query i iff j <= i" (src/attention.jl:112), key-padding mask,
+ *             query i iff j <= i" (src/attention.jl:76-81), key-padding mask,
  *             online softmax with a running max and denominator; saves
  *             lse = max + log(denominator) per query row;
  *   backward  src/attention_bwd.jl:1-175 -- P recomputed as exp(s - lse),

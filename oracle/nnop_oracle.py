@@ -14,7 +14,7 @@ functions in numpy, in float64, on inputs already rounded to the kernel dtype:
 * attention forward  -- ``test/attention_testsetup.jl:21-45`` (``naive_attention``)
   with the key-padding term ``log(mask)`` of ``test/attention_testsetup.jl:16-19``
   and GQA expansion ``d l h -> d l (num_q_per_kv h)`` (``:24-30``);
-  the attention scale is ``T(1/sqrt(E))`` as in ``src/attention.jl:198``.
+  the attention scale is ``T(1/sqrt(E))`` as in ``src/attention.jl:166``.
 * attention backward -- the closed-form rules the reference kernel implements
   (``src/attention_bwd.jl:87-169``): P = softmax(S), dV = Pᵀ dO,
   dP = dO Vᵀ, dS = P ∘ (dP − rowsum(dO ∘ O)), dpair = dS, dQ = scale·dS K,
@@ -24,12 +24,12 @@ functions in numpy, in float64, on inputs already rounded to the kernel dtype:
 * online softmax     -- ``test/softmax_tests.jl:6-10``; backward
   ``src/softmax.jl:70-80``.
 * rms_norm           -- ``test/rmsnorm_tests.jl:7-9``; backward
-  ``src/rms_norm.jl:126-191``.
+  ``src/rms_norm.jl:43-115``.
 * layer_norm         -- ``test/layernorm_tests.jl:7-11``; backward
   ``src/layer_norm.jl:97-137``.
-* llama_rope         -- the kernel ``src/rope/llama_rope.jl:244-285`` (which uses
+* llama_rope         -- the kernel ``src/rope/llama_rope.jl:24-65`` (which uses
   cos/sin of the first half of the embedding for both halves) and
-  ``LlamaRotaryEmbedding`` ``src/rope/llama_rope.jl:227-242``.
+  ``LlamaRotaryEmbedding`` ``src/rope/llama_rope.jl:7-22``.
 
 Array layout
 ------------
@@ -97,7 +97,7 @@ def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
 
 def attention_scale(E: int, dtype: str) -> float:
     """``scale = T(inv(sqrt(QE)))`` -- the scale rounded to the kernel dtype
-    (``src/attention.jl:198``, ``src/attention_bwd.jl:235``)."""
+    (``src/attention.jl:166``, ``src/attention_bwd.jl:235``)."""
     return float(round_to(np.array([1.0 / np.sqrt(E)]), dtype)[0])
 
 
@@ -136,7 +136,7 @@ def _logits(q, k, pair, causal, kpad_mask, scale):
     s = np.einsum("bhqe,bhke->bhqk", q, kk, optimize=True) * q.dtype.type(scale)
     if causal:
         # NNlib make_causal_mask: key j is visible to query i iff j <= i
-        # (top-left aligned), src/attention.jl:112.
+        # (top-left aligned), src/attention.jl:76-81.
         qi = np.arange(QL)[:, None]
         kj = np.arange(KL)[None, :]
         s = np.where(kj <= qi, s, s.dtype.type(-np.inf))
@@ -259,7 +259,7 @@ def rms_norm_fwd(x, w, *, eps=1e-6, offset=0.0):
 
 def rms_norm_bwd(dy, x, w, *, eps=1e-6, offset=0.0):
     """dx = rstd·m − rstd³/N·(Σ m∘x)·x with m = Δ∘(w+offset);
-    dw = Σ_rows Δ∘x·rstd (``src/rms_norm.jl:126-191``)."""
+    dw = Σ_rows Δ∘x·rstd (``src/rms_norm.jl:43-115``)."""
     dy = np.asarray(dy, np.float64)
     x = np.asarray(x, np.float64)
     w = np.asarray(w, np.float64)
@@ -306,7 +306,7 @@ def layer_norm_bwd(dy, x, w, *, eps=1e-6):
 
 def llama_rotary_embedding(dim: int, position_ids, base: int = 10000):
     """``LlamaRotaryEmbedding(dim; base)(position_ids)``
-    (``src/rope/llama_rope.jl:227-242``), evaluated in float32 like Julia.
+    (``src/rope/llama_rope.jl:7-22``), evaluated in float32 like Julia.
 
     position_ids: (B, L) float32.  Returns ``(cos, sin)`` of shape (B, L, dim)
     float32."""
@@ -328,12 +328,12 @@ def _rope(x, cos, sin, sign):
 
 
 def rope_fwd(q, k, cos, sin):
-    """``llama_rope`` (kernel ``src/rope/llama_rope.jl:263-281``): pairs
+    """``llama_rope`` (kernel ``src/rope/llama_rope.jl:45-61``): pairs
     (i, i+E/2) are rotated with cos/sin of index i (first half)."""
     return _rope(q, cos, sin, 1.0), _rope(k, cos, sin, 1.0)
 
 
 def rope_bwd(dq, dk, cos, sin):
     """``∇llama_rope`` = the same kernel with ``sin_sign = -1``
-    (``src/rope/llama_rope.jl:306,312``)."""
+    (``src/rope/llama_rope.jl:86,92``)."""
     return _rope(dq, cos, sin, -1.0), _rope(dk, cos, sin, -1.0)

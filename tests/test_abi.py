@@ -1,6 +1,6 @@
 """CPU checks of the C-ABI library: it loads without a GPU, exports every entry
 point declared in include/nnop_b200.h, and rejects invalid shapes before any
-launch with the reference's error text (src/attention.jl:185-188)."""
+launch with the reference's error text (src/attention.jl:153-156)."""
 import ctypes as C
 import pathlib
 import re
