@@ -2,6 +2,7 @@
 point declared in include/nnop_b200.h, and rejects invalid shapes before any
 launch with the reference's error text (src/attention.jl:153-156)."""
 import ctypes as C
+import os
 import pathlib
 import re
 import subprocess
@@ -102,6 +103,15 @@ def test_no_cpu_fallback():
         nnop.online_softmax(x)
     with pytest.raises(nnop.NNopError, match="CUDA tensors only"):
         nnop.flash_attention(torch.ones(1, 1, 4, 16), torch.ones(1, 1, 4, 16), torch.ones(1, 1, 4, 16), causal=False)
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """Without the compiled library the package does not import (no host path to fall back to)."""
+    import sys
+    code = "import nnop"
+    env = dict(os.environ, NNOP_B200_LIB=str(tmp_path / "absent.so"), PYTHONPATH=str(ROOT / "onionop.jl_b200"))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0 and "absent.so" in r.stderr
 
 
 def test_product_does_not_import_oracle():
