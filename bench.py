@@ -580,7 +580,9 @@ def run_ours(args):
     del o, lse, ws
     torch.cuda.empty_cache()
     host_in = [x.to("cpu").pin_memory() for x in (q, k, v, pair, do)]
-    host_out = [[torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in (q, k, v, pair)] for _ in range(2)]
+    # one pinned output set: the device->host copies run in order on one stream,
+    # so step k+1's copies land after step k's (the values are not read back)
+    host_out = [[torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in (q, k, v, pair)]]
     del q, k, v, pair, do
     torch.cuda.empty_cache()
     dev_in = [[torch.empty(x.shape, dtype=x.dtype, device=dev) for x in host_in] for _ in range(2)]
@@ -607,7 +609,7 @@ def run_ours(args):
             free[bi] = done
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done)
-                for h_, g_ in zip(host_out[bi], grads):
+                for h_, g_ in zip(host_out[0], grads):
                     g_.record_stream(s_out)
                     h_.copy_(g_, non_blocking=True)
         stream.wait_stream(s_out)
