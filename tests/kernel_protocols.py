@@ -1,0 +1,419 @@
+"""Randomised models of the mbarrier protocols of the tcgen05 attention kernels
+(onionop.jl_b200/csrc/fa_fwd_sm100.cu, fa_bwd_sm100.cu), for tests on the CPU.
+
+Each kernel role (TMA producer, MMA issuer, softmax / elementwise warpgroups,
+tile provider, dQ warps) is a generator that yields the waits and arrivals the
+kernel code performs, in the kernel's order.  The tensor pipe is an in-order
+queue (tcgen05 operations of one thread run in issue order; a commit arrives
+once everything issued before it is done), TMA loads and stores complete at
+random times, and a random scheduler interleaves everything.  Shared-memory
+buffers and TMEM column ranges carry tags of the data they hold: every read
+checks the tag it expects, every overwrite checks that the old data has been
+consumed.  A wait for phase k models the hardware's parity test: it passes
+once k+1 phases completed and is a hang if k+2 have (the parity repeats).
+
+The models restate the kernels' protocols by hand; a change to a kernel's
+barriers should be mirrored here.  `plant` removes one wait (a planted mistake,
+on the CPU) so the tests can check that the model notices.
+"""
+from __future__ import annotations
+
+import random
+
+
+class ProtocolBug(Exception):
+    pass
+
+
+class _Bar:
+    def __init__(self, name, count):
+        self.name, self.count, self.pending, self.done = name, count, 0, 0
+
+    def arrive(self):
+        self.pending += 1
+        if self.pending == self.count:
+            self.pending, self.done = 0, self.done + 1
+
+
+class _Sim:
+    def __init__(self, seed):
+        self.rng = random.Random(seed)
+        self.bars, self.mem, self.pipe, self.asyncs = {}, {}, [], []
+        self.executed = set()
+
+    def bar(self, name, count=1):
+        self.bars[name] = _Bar(name, count)
+
+    def expect(self, key, tag):
+        if self.mem.get(key) != tag:
+            raise ProtocolBug(f"{key}: expected {tag}, holds {self.mem.get(key)}")
+
+    def mma(self, op_id, fn):
+        self.pipe.append(("mma", op_id, fn))
+
+    def commit(self, bar):
+        self.pipe.append(("commit", bar))
+
+    def run(self, roles, max_steps=400000):
+        blocked = {n: None for n in roles}
+        finished = set()
+
+        def runnable(n):
+            w = blocked[n]
+            if w is None:
+                return True
+            if w[0] == "until":
+                return w[1]()
+            b, k = self.bars[w[0]], w[1]
+            if b.done >= k + 2:
+                raise ProtocolBug(f"{n}: phase overrun on {b.name} (waits phase {k}, {b.done} done)")
+            return b.done >= k + 1
+
+        for _ in range(max_steps):
+            c = [("role", n) for n in roles if n not in finished and runnable(n)]
+            if self.pipe:
+                c.append(("pipe", None))
+            if self.asyncs:
+                c.append(("async", None))
+            if not c:
+                if len(finished) == len(roles):
+                    return
+                raise ProtocolBug(f"deadlock: {[(n, blocked[n]) for n in roles if n not in finished]}")
+            kind, n = self.rng.choice(c)
+            if kind == "pipe":
+                op = self.pipe.pop(0)
+                if op[0] == "mma":
+                    op[2]()
+                    self.executed.add(op[1])
+                else:
+                    self.bars[op[1]].arrive()
+            elif kind == "async":
+                fn, b = self.asyncs.pop(self.rng.randrange(len(self.asyncs)))
+                fn()
+                if b is not None:
+                    self.bars[b].arrive()
+            else:
+                blocked[n] = None
+                try:
+                    a = next(roles[n])
+                except StopIteration:
+                    finished.add(n)
+                    continue
+                if a[0] == "wait":
+                    blocked[n] = (a[1], a[2])
+                elif a[0] == "until":
+                    blocked[n] = ("until", a[1])
+                elif a[0] == "arrive":
+                    self.bars[a[1]].arrive()
+                else:
+                    a[1]()
+        raise ProtocolBug("no progress")
+
+
+def _wait(plant, name, phase):
+    """A wait, unless it is the planted mistake."""
+    return ("do", lambda: None) if plant == name else ("wait", name, phase)
+
+
+# ------------------------------------------------------------------ forward
+def forward(n_kt: int, pair: bool, seed: int, rescale_p: float = 0.5, plant: str | None = None):
+    """fa_fwd_sm100_kernel: Q once; K/V 2-stage ring; pair tiles in a 3-slot ring
+    loaded two key tiles ahead; S in two TMEM buffers (P aliases its tile's S);
+    one softmax warpgroup; PV(j) after PFull(j); S(j+1) issued before waiting
+    PFull(j)."""
+    sim = _Sim(seed)
+    sim.bar("QFull")
+    for s in range(2):
+        for n in ("KFull", "VFull", "KVEmpty", "SFull", "PFull"):
+            sim.bar(f"{n}{s}")
+    for s in range(3):
+        sim.bar(f"PairFull{s}")
+        sim.bar(f"PairEmpty{s}")
+    for n in ("OStep", "OFinal", "MmaDone"):
+        sim.bar(n)
+    o = {"n": 0}
+
+    def producer():
+        yield ("do", lambda: None)
+        if n_kt == 0:
+            return
+        sim.asyncs.append((lambda: sim.mem.__setitem__("Q", "q"), "QFull"))
+
+        def load_pair(j):
+            slot = j % 3
+            if j >= 3:
+                yield _wait(plant, f"PairEmpty{slot}", j // 3 - 1)
+
+            def land(j=j, slot=slot):
+                if j >= 3 and ("S", j - 3) not in sim.executed:
+                    raise ProtocolBug(f"pair slot {slot} reloaded before S({j - 3}) read it")
+                sim.mem[f"pair{slot}"] = j
+            sim.asyncs.append((land, f"PairFull{slot}"))
+        if pair:
+            yield from load_pair(0)
+            if n_kt >= 2:
+                yield from load_pair(1)
+        for j in range(n_kt):
+            s = j % 2
+            if j >= 2:
+                yield _wait(plant, f"KVEmpty{s}", j // 2 - 1)
+
+            def land_kv(j=j, s=s):
+                if j >= 2 and ("PV", j - 2) not in sim.executed:
+                    raise ProtocolBug(f"K/V stage {s} reloaded before PV({j - 2}) read it")
+                sim.mem[f"K{s}"] = sim.mem[f"V{s}"] = j
+            sim.asyncs.append((land_kv, f"KFull{s}"))
+            sim.asyncs.append((lambda: None, f"VFull{s}"))
+            if pair and j + 2 < n_kt:
+                yield from load_pair(j + 2)
+
+    def mma():
+        if n_kt == 0:
+            yield ("do", lambda: None)
+            return
+        yield ("wait", "QFull", 0)
+
+        def issue_s(j):
+            s = j % 2
+            yield _wait(plant, f"KFull{s}", j // 2)
+            if pair:
+                yield _wait(plant, f"PairFull{j % 3}", j // 3)
+
+            def run(j=j, s=s):
+                sim.expect("Q", "q")
+                sim.expect(f"K{s}", j)
+                if pair:
+                    sim.expect(f"pair{j % 3}", j)
+                if j >= 2 and ("PV", j - 2) not in sim.executed:
+                    raise ProtocolBug(f"S({j}) overwrites P({j - 2}) before PV read it")
+                sim.mem[f"S{j & 1}"] = ("S", j)
+            sim.mma(("S", j), run)
+            if pair:
+                sim.commit(f"PairEmpty{j % 3}")
+            sim.commit(f"SFull{j & 1}")
+
+        yield from issue_s(0)
+        for j in range(n_kt):
+            if j + 1 < n_kt:
+                yield from issue_s(j + 1)
+            s = j % 2
+            yield _wait(plant, f"PFull{j & 1}", j >> 1)
+            yield ("wait", f"VFull{s}", j // 2)
+
+            def pv(j=j, s=s):
+                sim.expect(f"S{j & 1}", ("P", j))
+                sim.expect(f"V{s}", j)
+                if o["n"] != j:
+                    raise ProtocolBug(f"O holds {o['n']} products at PV({j})")
+                o["n"] += 1
+            sim.mma(("PV", j), pv)
+            sim.commit(f"KVEmpty{s}")
+            sim.commit("OStep")
+            if j == n_kt - 1:
+                sim.commit("OFinal")
+        sim.commit("MmaDone")
+        yield ("wait", "MmaDone", 0)
+
+    def softmax():
+        yield ("do", lambda: None)
+        for j in range(n_kt):
+            yield _wait(plant, f"SFull{j & 1}", j >> 1)
+
+            def sm(j=j):
+                sim.expect(f"S{j & 1}", ("S", j))
+                sim.mem[f"S{j & 1}"] = ("P", j)
+            yield ("do", sm)
+            if j > 0 and sim.rng.random() < rescale_p:
+                yield _wait(plant, "OStep", j - 1)
+
+                def resc(j=j):
+                    if o["n"] != j:
+                        raise ProtocolBug(f"O rescaled with {o['n']} products at key tile {j}")
+                yield ("do", resc)
+            yield ("arrive", f"PFull{j & 1}")
+        if n_kt:
+            yield _wait(plant, "OFinal", 0)
+
+            def fin():
+                if o["n"] != n_kt:
+                    raise ProtocolBug(f"O read with {o['n']} of {n_kt} products")
+            yield ("do", fin)
+
+    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax()})
+
+
+# ------------------------------------------------------------------ backward (E = 64)
+def backward(T: int, pair: bool, seed: int, plant: str | None = None):
+    """fa_bwd_sm100_kernel (E = 64): Q/dO 2-stage ring per 128-query tile; two
+    64-query halves with their own TMEM Sᵀ/dPᵀ and elementwise warpgroups;
+    products (dV, dK) per half, S(t+1, half) right behind them; per tile dQ
+    from the tile's dS buffer (2 buffers), drained by 4 dQ warps that then
+    stage fp32 rows in that buffer; with a pair bias the MMA warp TMA-stores
+    each dS half (bulk_wait_read<2> per half, <0> before the dQ commit) and the
+    pair arrives in a 3-slot ring of half tiles."""
+    sim = _Sim(seed)
+    for n, c in (("KVFull", 1), ("DQFull", 1), ("DQEmpty", 4), ("Final", 1)):
+        sim.bar(n, c)
+    for i in range(2):
+        for n, c in (("QFull", 1), ("QEmpty", 1), ("SFull", 1), ("PFull", 1), ("DSEmpty", 4), ("TileFull", 1),
+                     ("TileEmpty", 2)):
+            sim.bar(f"{n}{i}", c)
+    for i in range(3):
+        sim.bar(f"PairFull{i}")
+        sim.bar(f"PairEmpty{i}")
+    stored, drained, lse_reads, pair_reads, staged = set(), {}, {}, set(), set()
+
+    def producer():
+        yield ("do", lambda: None)
+        sim.asyncs.append((lambda: sim.mem.__setitem__("KV", "kv"), "KVFull"))
+        for t in range(T):
+            s = t & 1
+            if t >= 2:
+                yield _wait(plant, f"QEmpty{s}", (t >> 1) - 1)
+
+            def landq(t=t, s=s):
+                if t >= 2 and not {("P", t - 2, 0), ("P", t - 2, 1)} <= sim.executed:
+                    raise ProtocolBug(f"Q/dO stage {s} reloaded before the products of tile {t - 2}")
+                sim.mem[f"Q{s}"] = t
+            sim.asyncs.append((landq, f"QFull{s}"))
+            if pair:
+                for h in range(2):
+                    n = 2 * t + h
+                    if n >= 3:
+                        yield _wait(plant, f"PairEmpty{n % 3}", n // 3 - 1)
+
+                    def landp(n=n):
+                        if n >= 3 and (n - 3) not in pair_reads:
+                            raise ProtocolBug(f"pair slot {n % 3} reloaded before half {n - 3} read it")
+                        sim.mem[f"pair{n % 3}"] = n
+                    sim.asyncs.append((landp, f"PairFull{n % 3}"))
+
+    def mma():
+        yield ("wait", "KVFull", 0)
+        issued = []
+
+        def issue_s(t, h):
+            if h == 0:
+                yield _wait(plant, f"QFull{t & 1}", t >> 1)
+
+            def run(t=t, h=h):
+                sim.expect(f"Q{t & 1}", t)
+                if t > 0 and ("P", t - 1, h) not in sim.executed:
+                    raise ProtocolBug(f"S({t},{h}) overwrites P/dS before products({t - 1},{h})")
+                sim.mem[f"S{h}"] = ("S", t)
+            sim.mma(("S", t, h), run)
+            sim.commit(f"SFull{h}")
+
+        yield from issue_s(0, 0)
+        yield from issue_s(0, 1)
+        for t in range(T):
+            for h in range(2):
+                yield _wait(plant, f"PFull{h}", t)
+                if pair:
+                    def store(t=t, h=h):
+                        sim.expect(f"ds{t & 1}{h}", ("dS", t))
+                        issued.append((t, h))
+
+                        def done(k=(t, h)):
+                            sim.expect(f"ds{k[0] & 1}{k[1]}", ("dS", k[0]))
+                            stored.add(k)
+                        sim.asyncs.append((done, None))
+                    yield ("do", store)
+                    if plant != "bulk_wait_read2":
+                        yield ("until", lambda n=len(issued): all(k in stored for k in issued[:n - 2]))
+
+                def prod(t=t, h=h):
+                    sim.expect(f"S{h}", ("P", t))
+                    sim.expect(f"Q{t & 1}", t)
+                sim.mma(("P", t, h), prod)
+                if h == 1:
+                    sim.commit(f"QEmpty{t & 1}")
+                if t + 1 < T:
+                    yield from issue_s(t + 1, h)
+            if t > 0:
+                yield _wait(plant, "DQEmpty", t - 1)
+            if pair and plant != "bulk_wait_read0":
+                yield ("until", lambda n=len(issued): all(k in stored for k in issued[:n]))
+
+            def dq(t=t):
+                for h in range(2):
+                    sim.expect(f"ds{t & 1}{h}", ("dS", t))
+                if t > 0 and len(drained.get(t - 1, ())) < 4:
+                    raise ProtocolBug(f"dQ({t}) overwrites dQ({t - 1}) before it was drained")
+                sim.mem["DQ"] = t
+            sim.mma(("DQ", t), dq)
+            sim.commit("DQFull")
+        sim.commit("Final")
+        yield ("wait", "Final", 0)
+
+    def provider():
+        yield ("do", lambda: None)
+        for t in range(T):
+            if t >= 2:
+                yield _wait(plant, f"TileEmpty{t & 1}", (t >> 1) - 1)
+
+            def wr(t=t):
+                old = sim.mem.get(f"lse{t & 1}")
+                if old is not None and len(lse_reads.get(old, ())) < 2:
+                    raise ProtocolBug(f"lse/delta of tile {old} overwritten before both halves read them")
+                sim.mem[f"lse{t & 1}"] = t
+            yield ("do", wr)
+            yield ("arrive", f"TileFull{t & 1}")
+
+    def elementwise(h):
+        for t in range(T):
+            yield _wait(plant, f"TileFull{t & 1}", t >> 1)
+            yield _wait(plant, f"SFull{h}", t)
+            if t >= 2:
+                yield _wait(plant, f"DSEmpty{t & 1}", (t >> 1) - 1)
+            n = 2 * t + h
+            if pair:
+                yield _wait(plant, f"PairFull{n % 3}", n // 3)
+
+            def ew(t=t, h=h, n=n):
+                sim.expect(f"lse{t & 1}", t)
+                lse_reads.setdefault(t, set()).add(h)
+                sim.expect(f"S{h}", ("S", t))
+                if pair:
+                    sim.expect(f"pair{n % 3}", n)
+                    pair_reads.add(n)
+                old = sim.mem.get(f"ds{t & 1}{h}")
+                if old is not None and (old != ("stg", t - 2) or (t - 2) not in staged):
+                    raise ProtocolBug(f"dS buffer {t & 1} half {h} rewritten while it holds {old}")
+                sim.mem[f"S{h}"] = ("P", t)
+                sim.mem[f"ds{t & 1}{h}"] = ("dS", t)
+            yield ("do", ew)
+            yield ("arrive", f"TileEmpty{t & 1}")
+            if pair:
+                yield ("arrive", f"PairEmpty{n % 3}")
+            yield ("arrive", f"PFull{h}")
+
+    def dq_warp(w):
+        for t in range(T):
+            yield _wait(plant, "DQFull", t)
+
+            def rd(t=t, w=w):
+                sim.expect("DQ", t)
+                drained.setdefault(t, set()).add(w)
+            yield ("do", rd)
+            yield ("arrive", "DQEmpty")
+
+            def stage(t=t):
+                if ("DQ", t) not in sim.executed:
+                    raise ProtocolBug(f"staging into the dS buffer before dQ({t}) read it")
+                if pair and not {(t, 0), (t, 1)} <= stored:
+                    raise ProtocolBug(f"staging of tile {t} before its dS stores read the buffer")
+                for h in range(2):
+                    if sim.mem.get(f"ds{t & 1}{h}") not in (("dS", t), ("stg", t)):
+                        raise ProtocolBug(f"staging into dS buffer {t & 1} holding {sim.mem.get(f'ds{t & 1}{h}')}")
+                    sim.mem[f"ds{t & 1}{h}"] = ("stg", t)
+            yield ("do", stage)
+            if w == 3:
+                yield ("do", lambda t=t: staged.add(t))
+            yield ("arrive", f"DSEmpty{t & 1}")
+
+    roles = {"producer": producer(), "mma": mma(), "provider": provider(), "ew0": elementwise(0),
+             "ew1": elementwise(1)}
+    for w in range(4):
+        roles[f"dq{w}"] = dq_warp(w)
+    sim.run(roles)

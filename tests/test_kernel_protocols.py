@@ -1,0 +1,52 @@
+"""CPU checks of the tcgen05 attention kernels' barrier protocols (models in
+kernel_protocols.py): under random interleavings of all roles, random TMA
+latencies and an in-order tensor pipe, no role deadlocks, no wait sees its
+barrier two phases ahead (a parity hang on the GPU), and no buffer or TMEM
+range is overwritten before its consumer read it -- for every tile count up to
+6, with and without the pair bias.  Planted mistakes (one wait removed, on the
+CPU) are caught, so the models can fail."""
+import pytest
+
+import kernel_protocols as kp
+
+
+@pytest.mark.parametrize("pair", [False, True])
+def test_forward_protocol(pair):
+    for n_kt in range(0, 7):
+        for seed in range(60):
+            kp.forward(n_kt, pair, seed)
+
+
+@pytest.mark.parametrize("pair", [False, True])
+def test_backward_protocol(pair):
+    for tiles in range(1, 7):
+        for seed in range(40):
+            kp.backward(tiles, pair, seed)
+
+
+def _caught(fn, plant, **kw):
+    for seed in range(200):
+        try:
+            fn(seed=seed, plant=plant, **kw)
+        except kp.ProtocolBug:
+            return True
+    return False
+
+
+@pytest.mark.parametrize("plant", ["KVEmpty0", "KVEmpty1", "PairEmpty0", "PFull0", "SFull1", "KFull1", "OStep",
+                                   "OFinal", "PairFull1"])
+def test_forward_planted_mistake_is_caught(plant):
+    assert _caught(kp.forward, plant, n_kt=5, pair=True)
+
+
+@pytest.mark.parametrize("plant", ["QEmpty0", "DSEmpty0", "DQEmpty", "PairEmpty0", "bulk_wait_read0", "TileEmpty0",
+                                   "SFull1", "PFull1", "QFull1", "DQFull", "TileFull0", "PairFull1"])
+def test_backward_planted_mistake_is_caught(plant):
+    assert _caught(kp.backward, plant, T=5, pair=True)
+
+
+def test_backward_per_half_store_wait_is_implied():
+    """The MMA warp's bulk_wait_read<2> after each dS store is implied by the
+    bulk_wait_read<0> before every dQ commit (the model finds no hazard without
+    it): the store two halves back is always already read."""
+    assert not _caught(kp.backward, "bulk_wait_read2", T=5, pair=True)
