@@ -314,21 +314,9 @@ def cpu_memory_rows(reps: int = 3) -> dict:
             "sample": f"C restatement (oracle/cpu/memops_cpu.c), fp32, full shapes, mean of {reps} calls"}
 
 
-def run_memory_suite(args):
-    """The memory-bound sweep (rms_norm / layer_norm on x (4096, 65536) bf16 and fp32,
-    online_softmax on x (8192, 16384) fp32) and the RoPE of config 3 (q 32 heads,
-    k 8 heads, L = 8192, E = 128, bf16), fwd and bwd, on one GPU: achieved HBM
-    GB/s from the algorithmic bytes (each tensor read or written once) and CUDA
-    events over K launches; every input is larger than L2."""
+def _event_timer(dev, K, W):
+    """fn -> mean ms of K calls after W warm-ups, CUDA events on the current stream."""
     import torch
-
-    import nnop
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    hbm, _, src = peaks()
-    g = torch.Generator(device=dev)
-    g.manual_seed(5)
-    K, W = max(args.steps, 3), max(args.warmup, 3)
     stream = torch.cuda.current_stream(dev)
 
     def timed(fn):
@@ -342,11 +330,27 @@ def run_memory_suite(args):
         e1.record(stream)
         torch.cuda.synchronize(dev)
         return e0.elapsed_time(e1) / K
+    return timed
 
+
+def measure_memory(dev, K: int, W: int) -> dict:
+    """The memory-bound sweep (config 5: rms_norm / layer_norm on x (4096, 65536)
+    bf16 and fp32, online_softmax on x (8192, 16384) fp32) and the RoPE of
+    config 3 (q 32 heads, k 8 heads, L = 8192, E = 128, bf16), fwd and bwd:
+    achieved HBM GB/s from the algorithmic bytes (each tensor read or written
+    once) over CUDA events of K launches; every input is larger than L2."""
+    import torch
+
+    import nnop
+    hbm, _, _ = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    timed = _event_timer(dev, K, W)
     rows = {}
 
     def add(name, nbytes, ms):
-        rows[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / hbm}
+        rows[name] = {"ms": ms, "GB/s": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / hbm,
+                      "bytes": nbytes}
 
     emb, n = 4096, 65536
     for dt, tag in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
@@ -363,7 +367,7 @@ def run_memory_suite(args):
         add(f"layer_norm_bwd_{tag}", 3 * n * emb * es, timed(lambda: nnop.grad_layer_norm(dy, mu, rs, x, w)))
         del x, dy, y
         torch.cuda.empty_cache()
-    x = 2 * torch.randn(16384, 8192, device=dev, generator=g)
+    x = 4 * torch.randn(16384, 8192, device=dev, generator=g)
     y = nnop.online_softmax(x)
     dy = torch.randn_like(x)
     add("online_softmax_fwd_f32", 2 * x.numel() * 4, timed(lambda: nnop.online_softmax(x)))
@@ -380,16 +384,32 @@ def run_memory_suite(args):
     add("llama_rope_bwd_bf16", rb, timed(lambda: nnop.grad_llama_rope(q, k, cos=cos, sin=sin)))
     del q, k, cos, sin
     torch.cuda.empty_cache()
+    return rows
+
+
+MEMORY_CONFIG = {"norms": "x (4096, 65536) Julia = [65536][4096] rows, w (and b) (4096,); bf16 and fp32",
+                 "softmax": "x (8192, 16384) fp32 ~ N(0, sigma=4), dim 1",
+                 "rope": "q (128, 8192, 32, 4), k (128, 8192, 8, 4) bf16, cos/sin (128, 8192, 4) fp32"}
+
+
+def run_memory_suite(args):
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, _, src = peaks()
+    K, W = max(args.steps, 3), max(args.warmup, 3)
     out = {"suite": "memory", "unit": "GB/s", "peak": hbm, "peak_source": f"{src} hbm_gbs", "steps": K,
-           "warmup": W, "ops": rows,
-           "cpu_baseline": None if args.no_cpu else cpu_memory_rows(),
-           "config": {"norms": "x (4096, 65536) Julia = [65536][4096] rows, w (and b) (4096,)",
-                      "softmax": "x (8192, 16384) fp32, dim 1", "rope": "q (128, 8192, 32, 4), k (128, 8192, 8, 4) bf16"}}
+           "warmup": W, "ops": measure_memory(dev, K, W),
+           "cpu_baseline": None if args.no_cpu else cpu_memory_rows(), "config": MEMORY_CONFIG}
     print(json.dumps(out), flush=True)
 
 
-# --------------------------------------------------------------- other attention configs
-def run_configs_suite(args):
+# Nominal fp32 FMA rate of a B200 (148 SMs x 128 lanes x 2 flops x 1.965 GHz):
+# the bound of the fp32 SIMT attention path, which no MEASURED_PEAKS entry covers.
+FP32_SIMT_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
+def measure_configs(dev, K: int, W: int) -> dict:
     """The attention configurations beside the headline one, fwd + bwd through
     the public API on one GPU (CUDA events over K steps after W warm-ups):
       1  fp32 E=64 L=512 H=4 B=2, non-causal, no bias, q,k,v ~ U[0,1), dO = ones;
@@ -404,24 +424,8 @@ def run_configs_suite(args):
     import torch
 
     import nnop
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    _, tc, src = peaks()
-    K, W = max(args.steps, 3), max(args.warmup, 3)
-    stream = torch.cuda.current_stream(dev)
-
-    def timed(fn):
-        for _ in range(W):
-            fn()
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(K):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        return e0.elapsed_time(e1) / K
-
+    hbm, tc, _ = peaks()
+    timed = _event_timer(dev, K, W)
     rows = {}
     # config 1
     g = torch.Generator(device=dev)
@@ -435,7 +439,9 @@ def run_configs_suite(args):
         nnop.grad_flash_attention(do, o, lse, q, k, v, causal=False)
     ms = timed(step1)
     f = sum(cfg_flops(B, H, L, E, False))
-    rows["config1_fp32"] = {"ms": ms, "TFLOP/s": f / (ms / 1e3) / 1e12, "flops": f}
+    rows["config1_fp32"] = {"ms": ms, "TFLOP/s": f / (ms / 1e3) / 1e12, "flops": f, "bound": "latency (fp32 SIMT)",
+                            "frac": f / (ms / 1e3) / 1e12 / FP32_SIMT_TFLOPS,
+                            "peak": FP32_SIMT_TFLOPS, "peak_source": "nominal fp32 FMA rate"}
     del q, k, v, do
     # config 3
     g.manual_seed(3)
@@ -462,11 +468,15 @@ def run_configs_suite(args):
     ms_bwd = timed(lambda: nnop.grad_flash_attention(do, o3, lse3, qr, kr, v, causal=True))
     ms = timed(step3)
     f = 14.0 * B * QH * L * L * E * 0.5
-    rows["config3_gqa_rope_bf16"] = {"ms": ms, "attention_ms": ms_attn, "TFLOP/s": f / (ms / 1e3) / 1e12,
-                                      "attention_TFLOP/s": f / (ms_attn / 1e3) / 1e12,
-                                      "tensor_frac": f / (ms_attn / 1e3) / 1e12 / tc, "flops": f,
-                                      "fwd_ms": ms_fwd, "fwd_TFLOP/s": f / 3.5 / (ms_fwd / 1e3) / 1e12,
-                                      "bwd_ms": ms_bwd, "bwd_TFLOP/s": f / 3.5 * 2.5 / (ms_bwd / 1e3) / 1e12}
+    rope_bytes = 2 * (2 * (q.numel() + k.numel()) * 2 + 2 * cos.numel() * 4)
+    rows["config3_gqa_rope_bf16"] = {
+        "ms": ms, "TFLOP/s": f / (ms / 1e3) / 1e12, "flops": f, "bound": "tensor",
+        "frac": f / (ms / 1e3) / 1e12 / tc, "peak": tc, "peak_source": "measured bf16_tflops (burst)",
+        "attention_ms": ms_attn, "attention_TFLOP/s": f / (ms_attn / 1e3) / 1e12,
+        "attention_frac": f / (ms_attn / 1e3) / 1e12 / tc,
+        "fwd_ms": ms_fwd, "fwd_TFLOP/s": f / 3.5 / (ms_fwd / 1e3) / 1e12,
+        "bwd_ms": ms_bwd, "bwd_TFLOP/s": f / 3.5 * 2.5 / (ms_bwd / 1e3) / 1e12,
+        "rope_fwd_bwd_bytes": rope_bytes}
     del o3, lse3
     del q, k, v, do, qr, kr, cos, sin, pos
     torch.cuda.empty_cache()
@@ -488,11 +498,31 @@ def run_configs_suite(args):
     ms = timed(step4)
     f_eff = 14.0 * H * E * L * float(lens.sum())
     f_pad = 14.0 * B * H * L * L * E
-    rows["config4_varlen_pair_f16"] = {"ms": ms, "TFLOP/s_effective": f_eff / (ms / 1e3) / 1e12,
-                                       "TFLOP/s_padded": f_pad / (ms / 1e3) / 1e12, "flops_effective": f_eff,
-                                       "flops_padded": f_pad, "sum_len": int(lens.sum())}
+    # algorithmic bytes: the pair over the kept key range read by the forward
+    # and the backward, dpair written in full, q, k, v, o, dO, dq, dk, dv once
+    pair_kept = float(lens.sum()) * L * H * 2
+    nbytes = 2 * pair_kept + B * L * L * H * 2 + 8 * B * H * L * E * 2
+    rl = max(f_eff / (tc * 1e12), nbytes / (hbm * 1e9))
+    rows["config4_varlen_pair_f16"] = {
+        "ms": ms, "TFLOP/s_effective": f_eff / (ms / 1e3) / 1e12, "TFLOP/s_padded": f_pad / (ms / 1e3) / 1e12,
+        "flops_effective": f_eff, "flops_padded": f_pad, "sum_len": int(lens.sum()), "bound": "hbm",
+        "algorithmic_bytes": nbytes, "GB/s": nbytes / (ms / 1e3) / 1e9,
+        "frac": rl / (ms / 1e3), "peak": hbm, "peak_source": "measured hbm_gbs",
+        "tensor_frac_effective": f_eff / (ms / 1e3) / 1e12 / tc}
+    del q, k, v, do, pair, mask
+    torch.cuda.empty_cache()
+    return rows
+
+
+def run_configs_suite(args):
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _, tc, src = peaks()
+    K, W = max(args.steps, 3), max(args.warmup, 3)
     out = {"suite": "configs", "unit": "TFLOP/s", "tensor_peak_tflops": tc, "peak_source": f"{src} bf16_tflops",
-           "steps": K, "warmup": W, "configs": rows, "data": "synthetic, seeded by config index"}
+           "steps": K, "warmup": W, "configs": measure_configs(dev, K, W),
+           "data": "synthetic, seeded by config index"}
     print(json.dumps(out), flush=True)
 
 
@@ -663,6 +693,28 @@ def run_ours(args):
                    "sample": f"{text}, {dt_s:.1f} s"}
         except Exception as e:   # the GPU numbers above stand; say why the baseline is missing
             cpu = {"value": None, "unit": "TFLOP/s", "kind": "port", "unavailable": f"{type(e).__name__}: {e}"[:300]}
+    # The other BASELINE configurations (1, 3, 4, 5) on the same GPU, after the
+    # headline's timed region, at N = 1 only: each one's own CUDA-event timing,
+    # TFLOP/s or GB/s and roofline fraction, plus the memory ops' CPU baseline.
+    extra = None
+    del dev_in, host_in, host_out
+    if world == 1 and not args.no_extra:
+        torch.cuda.empty_cache()
+        Kx, Wx = max(3, min(K, 10)), max(3, min(args.warmup, 5))
+        extra = measure_configs(dev, Kx, Wx)
+        extra["config5_memory"] = {"ops": measure_memory(dev, Kx, Wx), "unit": "GB/s", "peak": hbm,
+                                   "peak_source": f"{src} hbm_gbs", "config": MEMORY_CONFIG,
+                                   "steps": Kx, "warmup": Wx}
+        if not args.no_cpu:
+            try:
+                extra["config5_memory"]["cpu_baseline"] = cpu_memory_rows()
+            except Exception as e:
+                extra["config5_memory"]["cpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    # step roofline of the headline: the larger of its tensor time and the time
+    # to move its algorithmic bytes (pair read by the forward and the backward,
+    # causal half each; dpair written in full; q, k, v, o, dO, dq, dk, dv)
+    step_bytes = 2 * c * B * L * L * H * 2 + B * L * L * H * 2 + 8 * B * H * L * E * 2
+    step_floor_ms = max((fwd_f + bwd_f) / (tc * 1e12), step_bytes / (hbm * 1e9)) * 1e3
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
@@ -678,8 +730,13 @@ def run_ours(args):
             # per step: pair_tiles, fa_fwd; preprocess, fa_bwd, dq convert, dpair_from_tiles
             "gpu_launches": K * 6,
             "roofline": roofline,
+            "step_roofline": {"bound": "hbm" if step_bytes / (hbm * 1e9) > (fwd_f + bwd_f) / (tc * 1e12) else "tensor",
+                              "algorithmic_bytes": step_bytes, "flops": fwd_f + bwd_f, "floor_ms": step_floor_ms,
+                              "frac": step_floor_ms / ms},
             "clocks": clk,
         }
+        if extra is not None:
+            out["configs"] = extra
         if cpu is not None:
             out["cpu_baseline"] = cpu
         print(json.dumps(out), flush=True)
@@ -694,6 +751,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the other BASELINE configurations (1, 3, 4, 5) that the N=1 line carries")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--suite", default="attention", choices=["attention", "memory", "configs"],
                     help="memory: the norm / softmax / RoPE sweep (norm and softmax shapes, RoPE of the GQA workload) "

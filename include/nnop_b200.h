@@ -240,7 +240,9 @@ int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w,
  * loads it until the process exits); emb may be at most 2^21 (2,097,152),
  * larger values return NNOP_ERR_SHAPE.  The first call on a device looks the
  * array's device address up (cudaGetSymbolAddress), so make that first call
- * before any stream capture on that device.  All calls on a device share the
+ * before any stream capture on that device; the address is kept with the
+ * device's context and looked up again after a device reset (a new context
+ * loads the array at a new address).  All calls on a device share the
  * one array: calls that can overlap on the GPU (different streams without
  * ordering between them) race on it and must be serialised by the caller.
  */

@@ -17,6 +17,8 @@
 //   sums a (n/4, emb) partial with `sum(dw; dims=1)`, src/rms_norm.jl:162-167).
 // * rows whose length is not a multiple of the 16-byte vector, or unaligned
 //   base pointers, take the same kernels with a vector width of one element.
+#include <cuda.h>
+
 #include "common.cuh"
 
 #include <mutex>
@@ -871,22 +873,47 @@ constexpr size_t kNoAllocScratchBytes = 8u << 20;   // 8 MiB: 2^21 fp32 partials
 constexpr int64_t kNoAllocScratchFloats = (int64_t)(kNoAllocScratchBytes / sizeof(float));
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
+// The current context of the calling thread (driver call reached through the
+// runtime's entry-point query, so the library needs no libcuda link).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CUcontext current_context() {
+    static CtxGetCurrentFn fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (CtxGetCurrentFn) nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(ptr);
+    }();
+    CUcontext c = nullptr;
+    if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
 // Device address of g_noalloc_scratch for the current device, looked up once
-// per device (the host-side symbol is only a stand-in, never a device pointer).
+// per device and context (the host-side symbol is only a stand-in, never a
+// device pointer).  A device reset gives the device a new primary context, in
+// which the module -- and the array -- is loaded again at another address;
+// the context recorded beside each cached address makes the next call look
+// the address up again instead of writing through the stale one.
 int noalloc_scratch(float** out) {
     static std::mutex mu;
     static float* addr[64] = {nullptr};
+    static CUcontext ctx[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return fail(NNOP_ERR_CUDA, "rms_norm_bwd_noalloc: no current CUDA device");
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[dev] == nullptr) {
+    const CUcontext cur = current_context();
+    if (addr[dev] == nullptr || cur == nullptr || cur != ctx[dev]) {
+        // the lookup also makes the device's primary context current
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || p == nullptr)
             return fail(NNOP_ERR_CUDA, std::string("rms_norm_bwd_noalloc: cudaGetSymbolAddress failed: ") +
                                            cudaGetErrorString(e));
         addr[dev] = static_cast<float*>(p);
+        ctx[dev] = current_context();
     }
     *out = addr[dev];
     return NNOP_OK;

@@ -8,6 +8,7 @@ ABI and compare it with the workspace entry point on two calls in a row (the
 second call sees the scratch the first one left behind).  The file is named
 so that pytest collects it last."""
 import ctypes as C
+import gc
 
 import numpy as np
 import pytest
@@ -57,7 +58,59 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, emb, n):
         assert isapprox(dw.double().cpu().numpy(), dw_ref.double().cpu().numpy(), **tol)
 
 
-def test_noalloc_rejects_rows_beyond_the_scratch():
+def test_noalloc_largest_emb_matches_workspace_entry_point():
+    """emb = 2^21, the largest the built-in scratch takes: one partial row fits,
+    so the whole dw comes from one CTA walking every row."""
+    import torch
+    import nnop
+    from nnop._lib import lib
+    emb, n = 1 << 21, 3
+    g = torch.Generator(device="cuda").manual_seed(21)
+    x = torch.randn(n, emb, device="cuda", generator=g)
+    w = 1 + 0.1 * torch.randn(emb, device="cuda", generator=g)
+    dy = torch.randn(n, emb, device="cuda", generator=g)
+    _, rstd = nnop._rms_norm(x, w)
+    for _ in range(2):
+        dx, dw, dx_ref, dw_ref = _call_both(lib, dy, x, w, rstd, 0.0, 0)
+        assert isapprox(dx.double().cpu().numpy(), dx_ref.double().cpu().numpy(), atol=1e-6, rtol=1e-6)
+        assert isapprox(dw.double().cpu().numpy(), dw_ref.double().cpu().numpy(), atol=1e-6, rtol=1e-6)
+
+
+def test_noalloc_allocates_no_device_memory():
+    """Around a warmed-up call, neither torch's allocator nor the device's free
+    memory (cudaMemGetInfo) changes: the entry point takes no memory."""
+    import torch
+    import nnop
+    from nnop._lib import lib
+    n, emb = 2000, 4096
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(n, emb, device="cuda", generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(emb, device="cuda", generator=g)).bfloat16()
+    dy = torch.randn(n, emb, device="cuda", generator=g).bfloat16()
+    _, rstd = nnop._rms_norm(x, w)
+    dx = torch.empty_like(x)
+    dw = torch.empty(emb, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        st = lib.nnop_rms_norm_bwd_noalloc(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(),
+                                           dx.data_ptr(), dw.data_ptr(), emb, n, 0.0, 2, stream)
+        assert st == 0, lib.nnop_last_error()
+
+    call()                                   # first call on the device: address lookup
+    torch.cuda.synchronize()
+    gc.collect()                             # tensors of earlier tests freed now, not during the calls
+    torch_before = torch.cuda.memory_allocated()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() <= torch_before
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+
+
+def test_noalloc_rejects_emb_beyond_the_scratch():
     from nnop._lib import lib
     d = C.c_void_p(256)   # never dereferenced: the size check fails first
     st = lib.nnop_rms_norm_bwd_noalloc(d, d, d, d, d, d, (1 << 21) + 1, 4, 0.0, 0, None)
