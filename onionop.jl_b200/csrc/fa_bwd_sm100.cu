@@ -98,55 +98,6 @@ struct Lay {
 };
 static_assert(Lay::kAlloc <= 227 * 1024, "shared memory");
 
-// Warp-uniform bounded wait: true only if every lane saw the phase complete
-// (guards warp-wide tcgen05.ld/st, which must not run divergent).
-__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* ab, int site) {
-    const bool ok = wait(bar, parity, ab, site);
-    return __all_sync(0xffffffffu, ok);
-}
-
-// Two packed 16-bit values -> float (exact)
-template <typename T>
-__device__ __forceinline__ float lo16(uint32_t w);
-template <typename T>
-__device__ __forceinline__ float hi16(uint32_t w);
-template <>
-__device__ __forceinline__ float lo16<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w << 16); }
-template <>
-__device__ __forceinline__ float hi16<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-template <>
-__device__ __forceinline__ float lo16<__half>(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)w)); }
-template <>
-__device__ __forceinline__ float hi16<__half>(uint32_t w) {
-    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
-}
-
-// 16 columns of Pᵀ and dSᵀ from 16 columns of Sᵀ and dPᵀ (and of the pair
-// bias, when PAIR); columns t outside [lo, hi) are masked (probability 0).
-template <typename T, bool PAIR, bool MASKED>
-__device__ __forceinline__ void elementwise16(const uint32_t (&sr)[16], const uint32_t (&dr)[16],
-                                              const uint32_t (&pw)[8], const float4 (&l4)[4],
-                                              const float4 (&d4)[4], float sl2, int lo, int hi, uint32_t (&pk)[8],
-                                              uint32_t (&dk)[8]) {
-    const float* lse = reinterpret_cast<const float*>(l4);
-    const float* del = reinterpret_cast<const float*>(d4);
-#pragma unroll
-    for (int t = 0; t < 16; t += 2) {
-        float pv[2], dv[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            float off = -lse[t + u];
-            if (PAIR) off = fmaf(u ? hi16<T>(pw[t >> 1]) : lo16<T>(pw[t >> 1]), kLog2e, off);
-            float pr = ex2(fmaf(__uint_as_float(sr[t + u]), sl2, off));
-            if (MASKED) pr = (t + u >= lo && t + u < hi) ? pr : 0.f;
-            pv[u] = pr;
-            dv[u] = pr * (__uint_as_float(dr[t + u]) - del[t + u]);
-        }
-        pk[t >> 1] = pack16<T>(pv[0], pv[1]);
-        dk[t >> 1] = pack16<T>(dv[0], dv[1]);
-    }
-}
-
 template <typename T, bool CAUSAL, bool PAIR, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -548,8 +499,14 @@ int dispatch_flags(const Params& p, const void* pt, void* dt, cudaStream_t s) {
 
 }  // namespace
 
+int sm100_bwd128(const Params& p, int dtype, bool causal, cudaStream_t s);
+
+// Shapes the tcgen05 backward kernels cover: E = 64 (with or without the pair
+// bias, this file) and E = 128 without it (fa_bwd128_sm100.cu); the others
+// use the mma.sync kernels.
 bool sm100_bwd_supported(const Params& p, int dtype) {
-    return (dtype == NNOP_BF16 || dtype == NNOP_F16) && p.E == kE;
+    if (dtype != NNOP_BF16 && dtype != NNOP_F16) return false;
+    return p.E == kE || (p.E == 128 && p.pair == nullptr);
 }
 
 int sm100_bwd_tile() { return kBN; }
@@ -563,6 +520,7 @@ int sm100_bwd_timeouts() {
 }
 
 int sm100_bwd(const Params& p, const void* pair_tiles, void* ds_tiles, int dtype, bool causal, cudaStream_t s) {
+    if (p.E == 128) return sm100_bwd128(p, dtype, causal, s);
     if (dtype == NNOP_BF16)
         return causal ? dispatch_flags<__nv_bfloat16, true>(p, pair_tiles, ds_tiles, s)
                       : dispatch_flags<__nv_bfloat16, false>(p, pair_tiles, ds_tiles, s);

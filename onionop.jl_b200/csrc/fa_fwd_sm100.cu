@@ -81,12 +81,6 @@ struct Layout {
     static constexpr int kAlloc = kTotal + 1024;                // slack for 1024-byte alignment
 };
 
-// Warp-uniform bounded wait: true only if every lane saw the phase complete.
-__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* ab, int site) {
-    const bool ok = wait(bar, parity, ab, site);
-    return __all_sync(kFull, ok);
-}
-
 template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "fa_common.cuh"
+#include "sm100.cuh"
 
 namespace nnop {
 namespace fa {
@@ -61,6 +63,57 @@ __device__ __forceinline__ void build_eye(uint8_t* eye, float c, int tid, int nt
 // Start address of K16 step kk of the shifted identity.
 __device__ __forceinline__ uint32_t eye_step(uint32_t eye, int kk) {
     return eye + (kk < 4 ? 64 * 128 : 0) + (kk & 3) * 32;
+}
+
+// Warp-uniform bounded wait: true only if every lane saw the phase complete
+// (guards warp-wide tcgen05.ld/st, which must not run divergent).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* ab, int site) {
+    const bool ok = sm100::wait(bar, parity, ab, site);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Two packed 16-bit values -> float (exact)
+template <typename T>
+__device__ __forceinline__ float lo16(uint32_t w);
+template <typename T>
+__device__ __forceinline__ float hi16(uint32_t w);
+template <>
+__device__ __forceinline__ float lo16<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w << 16); }
+template <>
+__device__ __forceinline__ float hi16<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+template <>
+__device__ __forceinline__ float lo16<__half>(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)w)); }
+template <>
+__device__ __forceinline__ float hi16<__half>(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+// Backward elementwise step on 16 score columns of one key row (keys on TMEM
+// lanes): Pᵀ = exp2(Sᵀ·scale·log2e + pairᵀ·log2e − lse) and dSᵀ = Pᵀ∘(dPᵀ − δ),
+// packed to 16 bits.  lse is in log2 units; columns t outside [lo, hi) are
+// masked (probability 0).  `pw`: the 16 pair values (packed), when PAIR.
+template <typename T, bool PAIR, bool MASKED>
+__device__ __forceinline__ void elementwise16(const uint32_t (&sr)[16], const uint32_t (&dr)[16],
+                                              const uint32_t (&pw)[8], const float4 (&l4)[4],
+                                              const float4 (&d4)[4], float sl2, int lo, int hi, uint32_t (&pk)[8],
+                                              uint32_t (&dk)[8]) {
+    const float* lse = reinterpret_cast<const float*>(l4);
+    const float* del = reinterpret_cast<const float*>(d4);
+#pragma unroll
+    for (int t = 0; t < 16; t += 2) {
+        float pv[2], dv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float off = -lse[t + u];
+            if (PAIR) off = fmaf(u ? hi16<T>(pw[t >> 1]) : lo16<T>(pw[t >> 1]), kLog2e, off);
+            float pr = ex2(fmaf(__uint_as_float(sr[t + u]), sl2, off));
+            if (MASKED) pr = (t + u >= lo && t + u < hi) ? pr : 0.f;
+            pv[u] = pr;
+            dv[u] = pr * (__uint_as_float(dr[t + u]) - del[t + u]);
+        }
+        pk[t >> 1] = pack16<T>(pv[0], pv[1]);
+        dk[t >> 1] = pack16<T>(dv[0], dv[1]);
+    }
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -36,7 +36,11 @@ class _Bar:
 
 
 class _Sim:
-    def __init__(self, seed):
+    def __init__(self, seed, slow_tma: bool = False):
+        # slow_tma: a copy in flight lands only rarely while anything else can
+        # run (long TMA latencies), which exposes waits on copies that the
+        # uniform schedule would nearly always find already landed.
+        self.slow_tma = slow_tma
         self.rng = random.Random(seed)
         self.bars, self.mem, self.pipe, self.asyncs = {}, {}, [], []
         self.executed = set()
@@ -79,6 +83,8 @@ class _Sim:
                 if len(finished) == len(roles):
                     return
                 raise ProtocolBug(f"deadlock: {[(n, blocked[n]) for n in roles if n not in finished]}")
+            if self.slow_tma and len(c) > 1 and c[-1][0] == "async" and self.rng.random() < 0.97:
+                c.pop()
             kind, n = self.rng.choice(c)
             if kind == "pipe":
                 op = self.pipe.pop(0)
@@ -416,4 +422,166 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None):
              "ew1": elementwise(1)}
     for w in range(4):
         roles[f"dq{w}"] = dq_warp(w)
+    sim.run(roles)
+
+
+# ------------------------------------------------------------------ backward (E = 128)
+def backward128(T: int, seed: int, plant: str | None = None, slow_tma: bool = False):
+    """fa_bwd128_sm100_kernel (E = 128, no pair): Q/dO 3-stage ring per 64-query
+    step; steps alternate between two elementwise warpgroups, each with its own
+    TMEM Sᵀ and dPᵀ buffers; the packed Pᵀ/dSᵀ overwrite the step's Sᵀ columns,
+    dQᵀ is written into the warpgroup's dPᵀ columns once the elementwise step is
+    done with them, and read out by 4 dQ warps that then stage fp32 boxes in the
+    warpgroup's dS buffer.  Per step: products (dV, dK) and dQᵀ behind PFull;
+    Sᵀ(t+2) right behind them; dPᵀ(t+2) after DQEmpty (dQᵀ(t) read)."""
+    sim = _Sim(seed, slow_tma)
+    sim.bar("KVFull")
+    sim.bar("Final")
+    for s in range(3):
+        sim.bar(f"QFull{s}")
+        sim.bar(f"QEmpty{s}")
+    for w in range(2):
+        for n, c in (("SFull", 1), ("PFull", 1), ("DQFull", 1), ("DQEmpty", 4), ("DSEmpty", 4), ("TileFull", 1),
+                     ("TileEmpty", 1)):
+            sim.bar(f"{n}{w}", c)
+    drained, lse_reads, ew_done = {}, set(), set()
+
+    def producer():
+        yield ("do", lambda: None)
+        if T == 0:
+            return
+        sim.asyncs.append((lambda: sim.mem.__setitem__("KV", "kv"), "KVFull"))
+        for t in range(T):
+            s = t % 3
+            if t >= 3:
+                yield _wait(plant, f"QEmpty{s}", t // 3 - 1)
+
+            def landq(t=t, s=s):
+                if t >= 3 and ("P", t - 3) not in sim.executed:
+                    raise ProtocolBug(f"Q/dO stage {s} reloaded before the products of step {t - 3}")
+                sim.mem[f"Q{s}"] = t
+            sim.asyncs.append((landq, f"QFull{s}"))
+
+    def mma():
+        if T == 0:
+            yield ("do", lambda: None)
+        else:
+            yield ("wait", "KVFull", 0)
+
+        def score(t, dp):
+            w = t & 1
+
+            def run(t=t, w=w, dp=dp):
+                sim.expect("KV", "kv")
+                sim.expect(f"Q{t % 3}", t)
+                if dp:
+                    if t >= 2 and len(drained.get(t - 2, ())) < 4:
+                        raise ProtocolBug(f"dP({t}) overwrites dQ({t - 2}) before it was drained")
+                    sim.mem[f"DP{w}"] = ("dP", t)
+                else:
+                    if t >= 2 and ("P", t - 2) not in sim.executed:
+                        raise ProtocolBug(f"S({t}) overwrites P/dS({t - 2}) before the products read them")
+                    sim.mem[f"S{w}"] = ("S", t)
+            sim.mma(("dP" if dp else "S", t), run)
+
+        for t in range(min(T, 2)):
+            yield _wait(plant, f"QFull{t % 3}", t // 3)
+            score(t, False)
+            score(t, True)
+            sim.commit(f"SFull{t & 1}")
+        for t in range(T):
+            w = t & 1
+            yield _wait(plant, f"PFull{w}", t >> 1)
+
+            def prod(t=t, w=w):
+                sim.expect(f"S{w}", ("P", t))
+                sim.expect(f"Q{t % 3}", t)
+            sim.mma(("P", t), prod)
+            sim.commit(f"QEmpty{t % 3}")
+
+            def dq(t=t, w=w):
+                sim.expect(f"ds{w}", ("dS", t))
+                if t not in ew_done:
+                    raise ProtocolBug(f"dQ({t}) overwrites dP({t}) before the elementwise step read it")
+                sim.mem[f"DP{w}"] = ("dQ", t)
+            sim.mma(("DQ", t), dq)
+            sim.commit(f"DQFull{w}")
+            if t + 2 < T:
+                yield _wait(plant, f"QFull{(t + 2) % 3}", (t + 2) // 3)
+                score(t + 2, False)
+                yield _wait(plant, f"DQEmpty{w}", t >> 1)
+                score(t + 2, True)
+                sim.commit(f"SFull{w}")
+        sim.commit("Final")
+        yield ("wait", "Final", 0)
+
+    def provider():
+        yield ("do", lambda: None)
+        for t in range(T):
+            w = t & 1
+            if t >= 2:
+                yield _wait(plant, f"TileEmpty{w}", (t >> 1) - 1)
+
+            def wr(t=t, w=w):
+                old = sim.mem.get(f"lse{w}")
+                if old is not None and old not in lse_reads:
+                    raise ProtocolBug(f"lse/delta of step {old} overwritten before its warpgroup read them")
+                sim.mem[f"lse{w}"] = t
+            for _ in range(sim.rng.randrange(0, 40) if slow_tma else 0):   # global lse/delta loads in flight
+                yield ("do", lambda: None)
+            yield ("do", wr)
+            yield ("arrive", f"TileFull{w}")
+
+    def elementwise(w):
+        yield ("do", lambda: None)
+        for t in range(w, T, 2):
+            n = t >> 1
+            yield _wait(plant, f"TileFull{w}", n)
+            yield _wait(plant, f"SFull{w}", n)
+            if n >= 1:
+                yield _wait(plant, f"DSEmpty{w}", n - 1)
+
+            def ew(t=t, w=w):
+                sim.expect(f"lse{w}", t)
+                lse_reads.add(t)
+                sim.expect(f"S{w}", ("S", t))
+                sim.expect(f"DP{w}", ("dP", t))
+                old = sim.mem.get(f"ds{w}")
+                if old is not None and old != ("stg", t - 2, 4):
+                    raise ProtocolBug(f"dS buffer {w} rewritten while it holds {old}")
+                sim.mem[f"S{w}"] = ("P", t)
+                sim.mem[f"ds{w}"] = ("dS", t)
+                ew_done.add(t)
+            yield ("do", ew)
+            yield ("arrive", f"TileEmpty{w}")
+            yield ("arrive", f"PFull{w}")
+
+    def dq_warp(wi):
+        for t in range(T):
+            w = t & 1
+            yield _wait(plant, f"DQFull{w}", t >> 1)
+
+            def rd(t=t, w=w, wi=wi):
+                sim.expect(f"DP{w}", ("dQ", t))
+                drained.setdefault(t, set()).add(wi)
+            yield ("do", rd)
+            yield ("arrive", f"DQEmpty{w}")
+
+            def stage(t=t, w=w):
+                if ("DQ", t) not in sim.executed:
+                    raise ProtocolBug(f"staging into dS buffer {w} before dQ({t}) read it")
+                cur = sim.mem.get(f"ds{w}")
+                if cur == ("dS", t):
+                    sim.mem[f"ds{w}"] = ("stg", t, 1)
+                elif isinstance(cur, tuple) and cur[:2] == ("stg", t):
+                    sim.mem[f"ds{w}"] = ("stg", t, cur[2] + 1)
+                else:
+                    raise ProtocolBug(f"staging of step {t} into dS buffer {w} holding {cur}")
+            yield ("do", stage)
+            yield ("arrive", f"DSEmpty{w}")
+
+    roles = {"producer": producer(), "mma": mma(), "provider": provider(), "ew0": elementwise(0),
+             "ew1": elementwise(1)}
+    for wi in range(4):
+        roles[f"dq{wi}"] = dq_warp(wi)
     sim.run(roles)

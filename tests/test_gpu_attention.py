@@ -119,6 +119,20 @@ def test_attention_gqa(dtype, QH, KVH, causal):
             check(got, want, dtype, tag=f"E={E} L={L}")
 
 
+# E = 128 without a pair bias: the GQA workload's shape family (tcgen05 backward
+# with E on the TMEM lanes for dQ), causal and not, ragged lengths, key mask
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("QH,KVH", [(4, 1), (8, 2), (6, 3), (2, 2)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_gqa_e128(dtype, QH, KVH, causal):
+    for (QL, KL, use_mask) in [(255, 255, False), (256, 256, True), (513, 513, False), (100, 300, True),
+                               (300, 100, False), (64, 64, False), (1, 129, True)]:
+        if causal and QL != KL and (QL, KL) != (100, 300):
+            continue
+        got, want = run_case(2, QH, KVH, QL, KL, 128, dtype, causal, False, use_mask, seed=QH * 100 + QL + KL)
+        check(got, want, dtype, tag=f"QL={QL} KL={KL} mask={use_mask}")
+
+
 def test_attention_gqa_e128_pair_mask():
     for dtype in ("bf16", "f16", "f32"):
         got, want = run_case(2, 8, 2, 300, 300, 128, dtype, True, True, True, seed=5)

@@ -50,3 +50,17 @@ def test_backward_per_half_store_wait_is_implied():
     bulk_wait_read<0> before every dQ commit (the model finds no hazard without
     it): the store two halves back is always already read."""
     assert not _caught(kp.backward, "bulk_wait_read2", T=5, pair=True)
+
+
+@pytest.mark.parametrize("slow_tma", [False, True])
+def test_backward128_protocol(slow_tma):
+    for steps in range(0, 9):
+        for seed in range(40):
+            kp.backward128(steps, seed, slow_tma=slow_tma)
+
+
+@pytest.mark.parametrize("plant", ["QEmpty0", "QEmpty2", "QFull1", "QFull2", "PFull0", "PFull1", "SFull1",
+                                   "DQEmpty0", "DQEmpty1", "DQFull1", "DSEmpty0", "DSEmpty1", "TileFull0",
+                                   "TileEmpty1"])
+def test_backward128_planted_mistake_is_caught(plant):
+    assert _caught(kp.backward128, plant, T=7) or _caught(kp.backward128, plant, T=7, slow_tma=True)
