@@ -514,6 +514,56 @@ def measure_configs(dev, K: int, W: int) -> dict:
     return rows
 
 
+def measure_config3_sharded(dev, rank: int, world: int, K: int, W: int, barrier) -> float:
+    """Config 3 (GQA + RoPE, bf16, E=128, L=8192, QH=32, KH=8, B=4, causal) split
+    over the ranks by (batch, kv head) units (nnop.shards.shard_batch_heads):
+    strong scaling, the whole job fixed.  Each rank makes only its own pieces'
+    inputs (seeded by config and piece) and runs, per step and per piece, RoPE,
+    attention fwd + bwd and the RoPE backward; no collective on the data path.
+    Returns this rank's mean ms per step (CUDA events, barrier on both sides)."""
+    import torch
+
+    import nnop
+    from nnop import shards
+    B, QH, KH, L, E = 4, 32, 8, 8192, 128
+    n_rep = QH // KH
+    runs = []
+    for piece in shards.shard_batch_heads(B, KH, rank, world):
+        b0, b1, h0, h1 = piece
+        g = torch.Generator(device=dev)
+        g.manual_seed(3000 + 97 * b0 + h0)
+        nb, nh = b1 - b0, h1 - h0
+        q = torch.randn(nb, nh * n_rep, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+        k = torch.randn(nb, nh, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+        v = torch.randn(nb, nh, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+        do = torch.ones_like(q)
+        pos = torch.arange(L, device=dev, dtype=torch.float32).repeat(nb, 1)
+        cos, sin = nnop.LlamaRotaryEmbedding(E)(pos)
+        runs.append((q, k, v, do, cos, sin))
+
+    def step():
+        for q, k, v, do, cos, sin in runs:
+            qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
+            o, lse = nnop._flash_attention(qr, kr, v, causal=True)
+            dq, dk, _, _ = nnop.grad_flash_attention(do, o, lse, qr, kr, v, causal=True)
+            nnop.grad_llama_rope(dq, dk, cos=cos, sin=sin)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    del runs
+    torch.cuda.empty_cache()
+    return e0.elapsed_time(e1) / K
+
+
 def run_configs_suite(args):
     import torch
     dev = torch.device("cuda", 0)
@@ -710,6 +760,17 @@ def run_ours(args):
                 extra["config5_memory"]["cpu_baseline"] = cpu_memory_rows()
             except Exception as e:
                 extra["config5_memory"]["cpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    if world > 1 and not args.no_extra:
+        # the GQA workload over the same ranks, split by (batch, kv head) units
+        Kx, Wx = max(3, min(K, 10)), max(3, min(args.warmup, 5))
+        ms3 = max_over_ranks([measure_config3_sharded(dev, rank, world, Kx, Wx, barrier)], dev, world)[0]
+        f3 = 14.0 * 4 * 32 * 8192 * 8192 * 128 * 0.5
+        extra = {"config3_sharded": {
+            "ms": ms3, "TFLOP/s": f3 / (ms3 / 1e3) / 1e12, "flops": f3, "scaling": "strong",
+            "frac": f3 / (ms3 / 1e3) / 1e12 / (tc * world), "peak": tc * world,
+            "peak_source": f"{src} bf16_tflops x {world} GPUs",
+            "parallelism": f"(batch, kv head) units: B=4 x KH=8 = 32 over {world} ranks, no collective",
+            "steps": Kx, "warmup": Wx}}
     # step roofline of the headline: the larger of its tensor time and the time
     # to move its algorithmic bytes (pair read by the forward and the backward,
     # causal half each; dpair written in full; q, k, v, o, dO, dq, dk, dv)

@@ -3,8 +3,10 @@
 Every op of the path is independent across its outer dimension, so a job is
 split into per-rank shards with no data exchange on the attention path:
 
-* attention shards by batch (and, for GQA, by groups of kv heads: the query
-  heads of one kv head stay together, so dK and dV need no cross-rank sum);
+* attention shards by (batch, kv head) units (``shard_batch_heads``): the
+  query heads of one kv head stay together, so dK and dV need no cross-rank
+  sum, and a workload with few batches (the GQA workload has B = 4) still
+  spreads over 8 GPUs by kv-head groups;
   with a key-padding mask the work of batch b grows with its key length
   len_b (the kernels skip key tiles past len_b), so ``balance_by_length``
   splits the batch by the total of len_b instead of by count;
@@ -25,7 +27,7 @@ import torch
 
 from . import grad_layer_norm, grad_rms_norm
 
-__all__ = ["row_shard", "balance_by_length", "allreduce_norm_grads",
+__all__ = ["row_shard", "balance_by_length", "shard_batch_heads", "piece_views", "allreduce_norm_grads",
            "grad_rms_norm_sharded", "grad_layer_norm_sharded"]
 
 
@@ -61,6 +63,59 @@ def balance_by_length(lens, world: int) -> list[list[int]]:
         out[r].append(b)
         heapq.heappush(heap, (load + lens[b], r))
     return [sorted(s) for s in out]
+
+
+def shard_batch_heads(B: int, KH: int, rank: int, world: int) -> list[tuple[int, int, int, int]]:
+    """This rank's share of an attention job, as pieces ``(b0, b1, h0, h1)``:
+    batches ``[b0, b1)`` x kv heads ``[h0, h1)`` (query heads
+    ``[h0·n_rep, h1·n_rep)``).
+
+    The job's units are its (batch, kv head) pairs in batch-major order; each
+    rank takes a contiguous run of them (``row_shard``: sizes differ by at most
+    one unit, so with B·KH divisible by the world size every rank gets the same
+    work).  A run is cut into at most three pieces, each a plain slice of the
+    (B, H, L, E) tensors: a partial batch (one batch, a range of kv heads),
+    whole batches (every kv head), a partial batch.  Every piece is an
+    independent attention call; no piece needs data of another rank."""
+    if B < 0 or KH <= 0:
+        raise ValueError(f"invalid job: B={B}, KH={KH}")
+    units = row_shard(B * KH, rank, world)
+    lo, hi = units.start, units.stop
+    out = []
+    if lo == hi:
+        return out
+    if lo % KH:                                    # leading partial batch
+        b, h0 = divmod(lo, KH)
+        h1 = min(KH, h0 + (hi - lo))
+        out.append((b, b + 1, h0, h1))
+        lo = b * KH + h1
+    if hi - lo >= KH:                              # whole batches
+        nb = (hi - lo) // KH
+        out.append((lo // KH, lo // KH + nb, 0, KH))
+        lo += nb * KH
+    if lo < hi:                                    # trailing partial batch
+        b = lo // KH
+        out.append((b, b + 1, 0, hi - lo))
+    return out
+
+
+def piece_views(piece, n_rep: int, q=None, k=None, v=None, pair=None):
+    """The slices of (B, H, L, E) tensors q / k, v and of a (B, KL, QL, QH)
+    pair bias that belong to one piece of ``shard_batch_heads``.  q, k, v views
+    are contiguous; the pair view is contiguous only for whole-batch pieces
+    (its head axis is innermost), so partial-batch pieces copy it."""
+    b0, b1, h0, h1 = piece
+    out = []
+    if q is not None:
+        out.append(q[b0:b1, h0 * n_rep:h1 * n_rep])
+    if k is not None:
+        out.append(k[b0:b1, h0:h1])
+    if v is not None:
+        out.append(v[b0:b1, h0:h1])
+    if pair is not None:
+        pv = pair[b0:b1, :, :, h0 * n_rep:h1 * n_rep]
+        out.append(pv if pv.is_contiguous() else pv.contiguous())
+    return out
 
 
 def _world(group) -> int:

@@ -117,3 +117,84 @@ def test_two_gloo_ranks_norm_grads(tmp_path):
         np.testing.assert_allclose(g["dw_ln"], dw_ln, rtol=2e-2, atol=5e-2)
         np.testing.assert_allclose(g["db_ln"], db_ln, rtol=2e-2, atol=5e-2)
     assert all((got[0][k] == got[1][k]).all() for k in ("dw_rms", "dw_ln", "db_ln"))
+
+
+def _attn_worker(rank, world, port, out_dir):
+    """One rank of an attention job sharded by (batch, kv head): the oracle's
+    forward and backward on this rank's pieces only, results sent to rank 0."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), LOCAL_RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    sys.path[:0] = [str(ROOT), str(ROOT / "onionop.jl_b200")]
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from nnop import shards
+    from oracle import nnop_oracle as orc
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        q, k, v, do, pair = _attn_job()
+        B, QH, L, E = q.shape
+        KH = k.shape[1]
+        n_rep = QH // KH
+        out = {}
+        for i, piece in enumerate(shards.shard_batch_heads(B, KH, rank, world)):
+            qs, ks, vs, ps = (t.numpy() for t in shards.piece_views(piece, n_rep, *map(torch.from_numpy,
+                                                                                    (q, k, v)), torch.from_numpy(pair)))
+            (dos,) = (t.numpy() for t in shards.piece_views(piece, n_rep, torch.from_numpy(do)))
+            o, _ = orc.attention_fwd(qs, ks, vs, ps, causal=True, scale=0.25)
+            g = orc.attention_bwd(dos, qs, ks, vs, ps, causal=True, scale=0.25)
+            for name, a in zip(("o", "dq", "dk", "dv", "dpair"), (o,) + tuple(g)):
+                out[f"{i}_{name}"] = a
+            out[f"{i}_piece"] = np.array(piece)
+        np.savez(pathlib.Path(out_dir) / f"attn{rank}.npz", **out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _attn_job():
+    import numpy as np
+    rng = np.random.default_rng(21)
+    B, QH, KH, L, E = 2, 8, 4, 12, 8
+    q = rng.standard_normal((B, QH, L, E))
+    k, v = rng.standard_normal((B, KH, L, E)), rng.standard_normal((B, KH, L, E))
+    do = rng.standard_normal((B, QH, L, E))
+    pair = rng.standard_normal((B, L, L, QH))
+    return q, k, v, do, pair
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_ranks_batch_head_shards_reassemble(tmp_path, world):
+    """Ranks that each run only their (batch, kv-head) pieces produce, put back
+    together, exactly the whole job's o, dq, dk, dv and dpair (GQA n_rep = 2,
+    causal, pair bias): the split needs no cross-rank reduction."""
+    import numpy as np
+    import torch.multiprocessing as mp
+
+    from oracle import nnop_oracle as orc
+    port = _free_port()
+    mp.start_processes(_attn_worker, args=(world, port, str(tmp_path)), nprocs=world, start_method="spawn",
+                       join=True)
+    q, k, v, do, pair = _attn_job()
+    n_rep = q.shape[1] // k.shape[1]
+    o_w, _ = orc.attention_fwd(q, k, v, pair, causal=True, scale=0.25)
+    dq_w, dk_w, dv_w, dp_w = orc.attention_bwd(do, q, k, v, pair, causal=True, scale=0.25)
+    got = {n: np.full_like(a, np.nan) for n, a in (("o", o_w), ("dq", dq_w), ("dk", dk_w), ("dv", dv_w),
+                                                     ("dpair", dp_w))}
+    for r in range(world):
+        f = np.load(tmp_path / f"attn{r}.npz")
+        i = 0
+        while f"{i}_piece" in f:
+            b0, b1, h0, h1 = f[f"{i}_piece"]
+            got["o"][b0:b1, h0 * n_rep:h1 * n_rep] = f[f"{i}_o"]
+            got["dq"][b0:b1, h0 * n_rep:h1 * n_rep] = f[f"{i}_dq"]
+            got["dk"][b0:b1, h0:h1] = f[f"{i}_dk"]
+            got["dv"][b0:b1, h0:h1] = f[f"{i}_dv"]
+            got["dpair"][b0:b1, :, :, h0 * n_rep:h1 * n_rep] = f[f"{i}_dpair"]
+            i += 1
+    for n, want in (("o", o_w), ("dq", dq_w), ("dk", dk_w), ("dv", dv_w), ("dpair", dp_w)):
+        assert not np.isnan(got[n]).any(), n          # every element produced by some rank
+        np.testing.assert_allclose(got[n], want, rtol=1e-12, atol=1e-12, err_msg=n)

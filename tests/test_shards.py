@@ -53,3 +53,40 @@ def test_allreduce_single_rank_is_identity():
     dw, db = torch.arange(4.0), torch.ones(4, dtype=torch.bfloat16)
     out = shards.allreduce_norm_grads(dw, db)
     assert out[0] is dw and out[1] is db
+
+
+@pytest.mark.parametrize("B,KH,world", [(4, 8, 8), (4, 8, 3), (2, 4, 3), (1, 4, 2), (4, 8, 1), (3, 5, 4), (1, 2, 4),
+                                        (8, 16, 8), (0, 4, 2)])
+def test_shard_batch_heads_covers_units_once(B, KH, world):
+    seen = []
+    sizes = []
+    for r in range(world):
+        pieces = shards.shard_batch_heads(B, KH, r, world)
+        assert len(pieces) <= 3
+        n = 0
+        for (b0, b1, h0, h1) in pieces:
+            assert 0 <= b0 < b1 <= B and 0 <= h0 < h1 <= KH
+            assert b1 - b0 == 1 or (h0, h1) == (0, KH)      # a partial batch is one batch
+            seen += [(b, h) for b in range(b0, b1) for h in range(h0, h1)]
+            n += (b1 - b0) * (h1 - h0)
+        sizes.append(n)
+    assert sorted(seen) == [(b, h) for b in range(B) for h in range(KH)]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_shard_batch_heads_gqa_workload_over_8():
+    """The GQA workload (B = 4, KH = 8): 8 ranks, each one batch x 4 kv heads."""
+    assert [shards.shard_batch_heads(4, 8, r, 8) for r in range(8)] == [
+        [(b, b + 1, h, h + 4)] for b in range(4) for h in (0, 4)]
+
+
+def test_piece_views_are_the_pieces_slices():
+    import torch
+    B, QH, KH, L, E = 2, 6, 3, 5, 4
+    q = torch.arange(B * QH * L * E, dtype=torch.float32).reshape(B, QH, L, E)
+    k = torch.arange(B * KH * L * E, dtype=torch.float32).reshape(B, KH, L, E)
+    pair = torch.arange(B * L * L * QH, dtype=torch.float32).reshape(B, L, L, QH)
+    qv, kv, vv, pv = shards.piece_views((1, 2, 1, 3), 2, q, k, k, pair)
+    assert torch.equal(qv, q[1:2, 2:6]) and qv.is_contiguous()
+    assert torch.equal(kv, k[1:2, 1:3]) and torch.equal(vv, kv)
+    assert torch.equal(pv, pair[1:2, :, :, 2:6]) and pv.is_contiguous()
