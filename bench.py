@@ -409,6 +409,55 @@ def run_memory_suite(args):
 FP32_SIMT_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
+def measure_config3(dev, K: int, W: int, B: int = 4) -> dict:
+    """Config 3: bf16 GQA E=128 L=8192 QH=32 KH=8 (B=4), causal: RoPE (positions
+    0..L-1, base 10000) on q and k, attention fwd + bwd (dO = ones), RoPE bwd;
+    the whole step, the attention alone, and its fwd and bwd separately (CUDA
+    events over K steps after W warm-ups).  FA2 flop convention."""
+    import torch
+
+    import nnop
+    _, tc, _ = peaks()
+    timed = _event_timer(dev, K, W)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    QH, KH, L, E = 32, 8, 8192, 128
+    q = torch.randn(B, QH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
+    do = torch.ones(B, QH, L, E, device=dev, dtype=torch.bfloat16)
+    pos = torch.arange(L, device=dev, dtype=torch.float32).repeat(B, 1)
+    cos, sin = nnop.LlamaRotaryEmbedding(E)(pos)
+
+    def attn3(qr, kr):
+        o, lse = nnop._flash_attention(qr, kr, v, causal=True)
+        return nnop.grad_flash_attention(do, o, lse, qr, kr, v, causal=True)
+
+    def step3():
+        qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
+        dq, dk, _, _ = attn3(qr, kr)
+        nnop.grad_llama_rope(dq, dk, cos=cos, sin=sin)
+    qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
+    ms_attn = timed(lambda: attn3(qr, kr))
+    ms_fwd = timed(lambda: nnop._flash_attention(qr, kr, v, causal=True))
+    o3, lse3 = nnop._flash_attention(qr, kr, v, causal=True)
+    ms_bwd = timed(lambda: nnop.grad_flash_attention(do, o3, lse3, qr, kr, v, causal=True))
+    ms = timed(step3)
+    f = 14.0 * B * QH * L * L * E * 0.5
+    rope_bytes = 2 * (2 * (q.numel() + k.numel()) * 2 + 2 * cos.numel() * 4)
+    out = {
+        "ms": ms, "TFLOP/s": f / (ms / 1e3) / 1e12, "flops": f, "bound": "tensor",
+        "frac": f / (ms / 1e3) / 1e12 / tc, "peak": tc, "peak_source": "measured bf16_tflops (burst)",
+        "attention_ms": ms_attn, "attention_TFLOP/s": f / (ms_attn / 1e3) / 1e12,
+        "attention_frac": f / (ms_attn / 1e3) / 1e12 / tc,
+        "fwd_ms": ms_fwd, "fwd_TFLOP/s": f / 3.5 / (ms_fwd / 1e3) / 1e12,
+        "bwd_ms": ms_bwd, "bwd_TFLOP/s": f / 3.5 * 2.5 / (ms_bwd / 1e3) / 1e12,
+        "rope_fwd_bwd_bytes": rope_bytes, "B": B}
+    del o3, lse3, q, k, v, do, qr, kr, cos, sin, pos
+    torch.cuda.empty_cache()
+    return out
+
+
 def measure_configs(dev, K: int, W: int) -> dict:
     """The attention configurations beside the headline one, fwd + bwd through
     the public API on one GPU (CUDA events over K steps after W warm-ups):
@@ -444,42 +493,7 @@ def measure_configs(dev, K: int, W: int) -> dict:
                             "peak": FP32_SIMT_TFLOPS, "peak_source": "nominal fp32 FMA rate"}
     del q, k, v, do
     # config 3
-    g.manual_seed(3)
-    B, QH, KH, L, E = 4, 32, 8, 8192, 128
-    q = torch.randn(B, QH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
-    k = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
-    v = torch.randn(B, KH, L, E, device=dev, dtype=torch.bfloat16, generator=g)
-    do = torch.ones(B, QH, L, E, device=dev, dtype=torch.bfloat16)
-    pos = torch.arange(L, device=dev, dtype=torch.float32).repeat(B, 1)
-    cos, sin = nnop.LlamaRotaryEmbedding(E)(pos)
-
-    def attn3(qr, kr):
-        o, lse = nnop._flash_attention(qr, kr, v, causal=True)
-        return nnop.grad_flash_attention(do, o, lse, qr, kr, v, causal=True)
-
-    def step3():
-        qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
-        dq, dk, _, _ = attn3(qr, kr)
-        nnop.grad_llama_rope(dq, dk, cos=cos, sin=sin)
-    qr, kr = nnop.llama_rope(q, k, cos=cos, sin=sin)
-    ms_attn = timed(lambda: attn3(qr, kr))
-    ms_fwd = timed(lambda: nnop._flash_attention(qr, kr, v, causal=True))
-    o3, lse3 = nnop._flash_attention(qr, kr, v, causal=True)
-    ms_bwd = timed(lambda: nnop.grad_flash_attention(do, o3, lse3, qr, kr, v, causal=True))
-    ms = timed(step3)
-    f = 14.0 * B * QH * L * L * E * 0.5
-    rope_bytes = 2 * (2 * (q.numel() + k.numel()) * 2 + 2 * cos.numel() * 4)
-    rows["config3_gqa_rope_bf16"] = {
-        "ms": ms, "TFLOP/s": f / (ms / 1e3) / 1e12, "flops": f, "bound": "tensor",
-        "frac": f / (ms / 1e3) / 1e12 / tc, "peak": tc, "peak_source": "measured bf16_tflops (burst)",
-        "attention_ms": ms_attn, "attention_TFLOP/s": f / (ms_attn / 1e3) / 1e12,
-        "attention_frac": f / (ms_attn / 1e3) / 1e12 / tc,
-        "fwd_ms": ms_fwd, "fwd_TFLOP/s": f / 3.5 / (ms_fwd / 1e3) / 1e12,
-        "bwd_ms": ms_bwd, "bwd_TFLOP/s": f / 3.5 * 2.5 / (ms_bwd / 1e3) / 1e12,
-        "rope_fwd_bwd_bytes": rope_bytes}
-    del o3, lse3
-    del q, k, v, do, qr, kr, cos, sin, pos
-    torch.cuda.empty_cache()
+    rows["config3_gqa_rope_bf16"] = measure_config3(dev, K, W)
     # config 4
     B, H, L, E = 16, 8, 4096, 64
     lens = np.random.default_rng(4).integers(256, L + 1, size=B)
@@ -512,6 +526,49 @@ def measure_configs(dev, K: int, W: int) -> dict:
     del q, k, v, do, pair, mask
     torch.cuda.empty_cache()
     return rows
+
+
+def measure_config2_per_head(dev, K: int, W: int) -> dict:
+    """The headline workload (config 2: bf16, E=64, L=4096, H=16, B=8, causal,
+    pair bias, dO = ones) through the per-head pair entry points: the bias and
+    dpair laid out (B, H, KL, QL), read and written in place by the tensor-core
+    kernels, with no re-layout pass.  CUDA events over K steps after W warm-ups."""
+    import torch
+
+    import nnop
+    E, L, H, B = CFG["E"], CFG["L"], CFG["H"], CFG["B"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(rank_seed(0))
+    q, k, v = (torch.randn(B, H, L, E, device=dev, dtype=torch.bfloat16, generator=g) for _ in range(3))
+    ph = torch.randn(B, H, L, L, device=dev, dtype=torch.bfloat16, generator=g)
+    do = torch.ones(B, H, L, E, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        o, lse = nnop._flash_attention_pair_per_head(q, k, v, ph, causal=True)
+        nnop.grad_flash_attention_pair_per_head(do, o, lse, q, k, v, ph, causal=True)
+    ms = _event_timer(dev, K, W)(step)
+    from nnop._lib import lib as _nnlib
+    import ctypes as _C
+    _nnlib.nnop_kernel_timing(1)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    _nnlib.nnop_kernel_timing(0)
+    kern = []
+    for which in (0, 1):
+        tot, cnt = _C.c_double(0.0), _C.c_int(0)
+        _nnlib.nnop_kernel_timing_read(which, _C.byref(tot), _C.byref(cnt))
+        kern.append(tot.value / cnt.value if cnt.value else float("nan"))
+    del q, k, v, ph, do
+    torch.cuda.empty_cache()
+    hbm, tc, _ = peaks()
+    fwd_f, bwd_f = cfg_flops(B, H, L, E, True)
+    nbytes = 2 * 0.5 * B * L * L * H * 2 + B * L * L * H * 2 + 8 * B * H * L * E * 2
+    floor = max((fwd_f + bwd_f) / (tc * 1e12), nbytes / (hbm * 1e9)) * 1e3
+    return {"ms": ms, "TFLOP/s": (fwd_f + bwd_f) / (ms / 1e3) / 1e12, "flops": fwd_f + bwd_f,
+            "algorithmic_bytes": nbytes, "floor_ms": floor, "frac": floor / ms, "bound": "hbm",
+            "fwd_kernel_ms": kern[0], "bwd_kernel_ms": kern[1],
+            "entry_points": "nnop_flash_attention_{fwd,bwd}_pair_per_head (pair (B, H, KL, QL))"}
 
 
 def measure_config3_sharded(dev, rank: int, world: int, K: int, W: int, barrier) -> float:
@@ -752,6 +809,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
         Kx, Wx = max(3, min(K, 10)), max(3, min(args.warmup, 5))
         extra = measure_configs(dev, Kx, Wx)
+        extra["config2_pair_per_head"] = measure_config2_per_head(dev, Kx, Wx)
         extra["config5_memory"] = {"ops": measure_memory(dev, Kx, Wx), "unit": "GB/s", "peak": hbm,
                                    "peak_source": f"{src} hbm_gbs", "config": MEMORY_CONFIG,
                                    "steps": Kx, "warmup": Wx}
@@ -815,9 +873,10 @@ def main():
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the other BASELINE configurations (1, 3, 4, 5) that the N=1 line carries")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--suite", default="attention", choices=["attention", "memory", "configs"],
+    ap.add_argument("--suite", default="attention", choices=["attention", "memory", "configs", "gqa"],
                     help="memory: the norm / softmax / RoPE sweep (norm and softmax shapes, RoPE of the GQA workload) "
-                         "on one GPU; configs: the fp32, GQA+RoPE and variable-length attention configurations")
+                         "on one GPU; configs: the fp32, GQA+RoPE and variable-length attention configurations; "
+                         "gqa: the GQA+RoPE configuration alone (--batch sets its B)")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override, for small profiler captures (the headline uses 8)")
     args = ap.parse_args()
@@ -829,6 +888,12 @@ def main():
         run_memory_suite(args)
     elif args.suite == "configs":
         run_configs_suite(args)
+    elif args.suite == "gqa":
+        import torch
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        out = measure_config3(dev, args.steps, args.warmup, B=args.batch or 4)
+        print(json.dumps({"suite": "gqa", "config3_gqa_rope_bf16": out}), flush=True)
     else:
         run_ours(args)
 

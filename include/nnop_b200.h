@@ -180,6 +180,50 @@ size_t nnop_flash_attention_bwd_workspace_size_reuse(int64_t E, int64_t QL, int6
                                                      int has_pair, size_t fwd_workspace_bytes,
                                                      int dtype);
 
+/*
+ * Forward with the pair bias laid out per head: pair [B][QH][KL][QL] (Julia
+ * pair (QL, KL, QH, B)) instead of the reference's head-innermost
+ * [B][KL][QL][QH].  It relaxes the layout of the reference's pair read
+ * (`_flash_attention_fwd!`, src/attention.jl:72); results are those of
+ * nnop_flash_attention_fwd on the same bias.  The tensor-core kernel reads
+ * the bias in place, so no workspace and no re-layout pass is needed.
+ *   dtype BF16 or F16; E = 64; QL a multiple of 8; all tensors 16-byte aligned.
+ *   −Inf bias entries are allowed only at keys kpad_mask removes (the bias
+ *   enters the scores through an identity matrix product, where 0·(−Inf)
+ *   would spread NaN over 16 queries of that key); mask other keys instead.
+ */
+int nnop_flash_attention_fwd_pair_per_head(const void* q, const void* k, const void* v,
+                                           const void* pair, const uint8_t* kpad_mask,
+                                           void* o, float* lse,
+                                           int64_t E, int64_t QL, int64_t KL,
+                                           int64_t QH, int64_t KH, int64_t B,
+                                           int causal, int dtype, void* stream);
+
+/* Bytes of workspace nnop_flash_attention_bwd_pair_per_head needs. */
+size_t nnop_flash_attention_bwd_pair_per_head_workspace_size(int64_t E, int64_t QL, int64_t KL,
+                                                             int64_t QH, int64_t KH, int64_t B,
+                                                             int dtype);
+
+/*
+ * Backward with the pair bias and dpair laid out per head ([B][QH][KL][QL]).
+ * It relaxes the layout of the reference's dpair (`∇flash_attention`,
+ * src/attention_bwd.jl:247-252, a head-innermost array zero-filled before the
+ * kernel): the backward kernel stores each dS tile straight into dpair and
+ * only the entries no tile covers (above the causal diagonal; keys past the
+ * last kept key) are zeroed, so every element is written once.  Arguments as
+ * nnop_flash_attention_bwd, with the restrictions of the forward above.
+ *   workspace: >= nnop_flash_attention_bwd_pair_per_head_workspace_size(...)
+ *   bytes, 256-byte aligned.
+ */
+int nnop_flash_attention_bwd_pair_per_head(const void* dO, const void* o, const float* lse,
+                                           const void* q, const void* k, const void* v,
+                                           const void* pair, const uint8_t* kpad_mask,
+                                           void* dq, void* dk, void* dv, void* dpair,
+                                           void* workspace, size_t workspace_bytes,
+                                           int64_t E, int64_t QL, int64_t KL,
+                                           int64_t QH, int64_t KH, int64_t B,
+                                           int causal, int dtype, void* stream);
+
 /* --------------------------------------------------------------------------
  * Online softmax over the contiguous axis (Julia dims=1)
  * -------------------------------------------------------------------------- */

@@ -394,3 +394,140 @@ int nnop_flash_attention_bwd(const void* dO, const void* o, const float* lse, co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Pair bias laid out per head.
+//
+// The reference takes the pair bias head-innermost, Julia (H, QL, KL, B)
+// (src/attention.jl:72), and returns dpair the same way, zero-filled first
+// (src/attention_bwd.jl:247-252).  The tcgen05 kernels read and write it per
+// head and key-major, so the drop-in entry points above move it through
+// re-layout passes (pair_tiles.cu).  A caller that can keep the bias per head,
+// Julia (QL, KL, H, B) = row-major [B][QH][KL][QL], uses these entry points
+// instead: the forward reads the bias with a 3-D tensor map, the backward
+// stores dS straight into dpair, and each CTA also zeroes the parts of its key
+// rows that no tile covers (above the causal diagonal, every query of a key
+// tile past the last kept key), so every element is written once.
+// bf16 / f16, E = 64, QL a multiple of 8 (16-byte rows).  The forward adds
+// the bias on the tensor cores (an identity UMMA), where 0·(−Inf) would turn
+// the 16 queries of a UMMA K block into NaN, so −Inf entries are allowed only
+// at keys the key-padding mask removes (their scores are discarded); express
+// other −Inf entries with the mask.  There is no mma.sync fallback:
+// NNOP_B200_FA does not apply here.
+// ---------------------------------------------------------------------------
+namespace nnop {
+namespace {
+
+int check_per_head(const char* what, int64_t E, int64_t QL, int64_t KL, int64_t QH, int64_t KH, int64_t B,
+                   int dtype) {
+    int st = check_dims(E, QL, KL, QH, KH, B, dtype);
+    if (st) return st;
+    if (dtype != NNOP_BF16 && dtype != NNOP_F16)
+        return fail(NNOP_ERR_DTYPE, std::string(what) + ": a per-head pair bias takes bf16 or f16");
+    if (E != 64) return fail(NNOP_ERR_SHAPE, std::string(what) + ": a per-head pair bias takes E = 64");
+    if (QL % 8 != 0)
+        return fail(NNOP_ERR_SHAPE, std::string(what) + ": a per-head pair bias needs QL a multiple of 8 (got " +
+                                        std::to_string(QL) + ")");
+    if ((KL + 31) / 32 > 2048) return fail(NNOP_ERR_SHAPE, std::string(what) + ": key length above 65536");
+    return NNOP_OK;
+}
+
+}  // namespace
+}  // namespace nnop
+
+extern "C" {
+
+int nnop_flash_attention_fwd_pair_per_head(const void* q, const void* k, const void* v, const void* pair,
+                                           const uint8_t* kpad_mask, void* o, float* lse, int64_t E, int64_t QL,
+                                           int64_t KL, int64_t QH, int64_t KH, int64_t B, int causal, int dtype,
+                                           void* stream) {
+    int st = check_per_head("flash_attention_fwd", E, QL, KL, QH, KH, B, dtype);
+    if (st) return st;
+    if (QL == 0 || B == 0) return NNOP_OK;
+    if (!q || !k || !v || !pair || !o || !lse) return fail(NNOP_ERR_ARG, "flash_attention_fwd: NULL pointer");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(pair))
+        return fail(NNOP_ERR_ALIGN, "flash_attention_fwd: q, k, v, pair, o must be 16-byte aligned");
+    fa::Params p{};
+    p.q = q; p.k = k; p.v = v; p.pair = pair; p.kmask = kpad_mask; p.o = o; p.lse = lse;
+    p.QL = QL; p.KL = KL; p.E = (int)E; p.QH = (int)QH; p.KH = (int)KH; p.B = (int)B;
+    p.n_rep = (int)(QH / KH);
+    p.pair_per_head = 1;
+    const float sc = (float)(1.0 / sqrt((double)E));
+    p.scale = dtype == NNOP_BF16 ? __bfloat162float(__float2bfloat16_rn(sc)) : __half2float(__float2half_rn(sc));
+    cudaStream_t s = (cudaStream_t)stream;
+    const int slot = timer_begin(0, s);
+    st = fa::sm100_fwd(p, nullptr, dtype, causal != 0, s);
+    timer_end(0, slot, s);
+    return st;
+}
+
+size_t nnop_flash_attention_bwd_pair_per_head_workspace_size(int64_t E, int64_t QL, int64_t KL, int64_t QH,
+                                                             int64_t KH, int64_t B, int dtype) {
+    (void)KH;
+    if (E <= 0 || QL < 0 || KL < 0 || QH <= 0 || B < 0) return 0;
+    return bwd_layout(nullptr, E, QL, KL, QH, B, false, false, dtype).bytes;
+}
+
+int nnop_flash_attention_bwd_pair_per_head(const void* dO, const void* o, const float* lse, const void* q,
+                                           const void* k, const void* v, const void* pair, const uint8_t* kpad_mask,
+                                           void* dq, void* dk, void* dv, void* dpair, void* workspace,
+                                           size_t workspace_bytes, int64_t E, int64_t QL, int64_t KL, int64_t QH,
+                                           int64_t KH, int64_t B, int causal, int dtype, void* stream) {
+    int st = check_per_head("flash_attention_bwd", E, QL, KL, QH, KH, B, dtype);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (QL == 0 || B == 0) {
+        // no queries: dk = dv = 0 (dpair is empty)
+        if (B > 0 && KL > 0 &&
+            (cudaMemsetAsync(dk, 0, (size_t)B * KH * KL * E * 2, s) != cudaSuccess ||
+             cudaMemsetAsync(dv, 0, (size_t)B * KH * KL * E * 2, s) != cudaSuccess))
+            return fail(NNOP_ERR_CUDA, "flash_attention_bwd: memset failed");
+        return NNOP_OK;
+    }
+    if (!dO || !o || !lse || !q || !k || !v || !pair || !dq || !dk || !dv || !dpair)
+        return fail(NNOP_ERR_ARG, "flash_attention_bwd: NULL pointer");
+    if (!aligned16(dO) || !aligned16(o) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dq) ||
+        !aligned16(dk) || !aligned16(dv) || !aligned16(pair) || !aligned16(dpair))
+        return fail(NNOP_ERR_ALIGN, "flash_attention_bwd: dense tensors must be 16-byte aligned");
+    BwdWorkspace ws = bwd_layout(workspace, E, QL, KL, QH, B, false, false, dtype);
+    if (!workspace || workspace_bytes < ws.bytes)
+        return fail(NNOP_ERR_WORKSPACE, "flash_attention_bwd: workspace too small (need " + std::to_string(ws.bytes) +
+                                            " bytes)");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return fail(NNOP_ERR_ALIGN, "flash_attention_bwd: workspace must be 256-byte aligned");
+    fa::Params p{};
+    p.q = q; p.k = k; p.v = v; p.pair = pair; p.kmask = kpad_mask; p.o = const_cast<void*>(o);
+    p.lse = const_cast<float*>(lse); p.dO = dO;
+    p.dq = dq; p.dk = dk; p.dv = dv; p.dpair = dpair;
+    p.QL = QL; p.KL = KL; p.E = (int)E; p.QH = (int)QH; p.KH = (int)KH; p.B = (int)B;
+    p.n_rep = (int)(QH / KH);
+    p.pair_per_head = 1;
+    p.delta = ws.delta;
+    p.kv_len = kpad_mask ? ws.kv_len : nullptr;
+    p.dq_acc = ws.dq_acc;
+    const float sc = (float)(1.0 / sqrt((double)E));
+    p.scale = dtype == NNOP_BF16 ? __bfloat162float(__float2bfloat16_rn(sc)) : __half2float(__float2half_rn(sc));
+    const int64_t rows = B * QH * QL;
+    if (kpad_mask && (st = fa_host::launch_kv_len(kpad_mask, ws.kv_len, KL, (int)B, s))) return st;
+    if (cudaMemsetAsync(ws.dq_acc, 0, (size_t)rows * E * sizeof(float), s) != cudaSuccess)
+        return fail(NNOP_ERR_CUDA, "flash_attention_bwd: memset failed");
+    const bool c = causal != 0;
+    if (dtype == NNOP_BF16) {
+        using T = __nv_bfloat16;
+        if ((st = fa_host::launch_preprocess<T>((const T*)dO, (const T*)o, ws.delta, rows, (int)E, s))) return st;
+        const int slot = timer_begin(1, s);
+        st = fa::sm100_bwd(p, nullptr, nullptr, dtype, c, s);
+        timer_end(1, slot, s);
+        if (st) return st;
+        return fa_host::launch_convert<T>(ws.dq_acc, (T*)dq, rows * E, s);   // dpair zeros: written by the kernel
+    }
+    using T = __half;
+    if ((st = fa_host::launch_preprocess<T>((const T*)dO, (const T*)o, ws.delta, rows, (int)E, s))) return st;
+    const int slot = timer_begin(1, s);
+    st = fa::sm100_bwd(p, nullptr, nullptr, dtype, c, s);
+    timer_end(1, slot, s);
+    if (st) return st;
+    return fa_host::launch_convert<T>(ws.dq_acc, (T*)dq, rows * E, s);
+}
+
+}  // extern "C"

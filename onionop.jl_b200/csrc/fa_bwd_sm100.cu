@@ -35,7 +35,8 @@
 //   warps 2-3   tile provider: lse (log2 units) and δ of the tile's queries
 //   warps 4-7   elementwise, query half 0 (one key per TMEM lane)
 //   warps 8-11  elementwise, query half 1
-//   warps 12-15 dQ: TMEM dQ rows -> staged fp32 boxes -> TMA reduce-add
+//   warps 12-15 dQ: TMEM dQ rows -> staged fp32 boxes -> TMA reduce-add;
+//               with a per-head dpair, warp 12 first writes its zeros
 // TMEM columns: Sᵀ half 0 [0,64), half 1 [64,128), dPᵀ half 0 [128,192),
 // half 1 [192,256), dV [256,320), dK [320,384), dQ [384,448).  The 16-bit
 // Pᵀ / dSᵀ of a half overwrite the first 32 columns of its own score buffers.
@@ -91,7 +92,9 @@ struct Lay {
     static constexpr int kPairSlot = kBN * kHM * 2;
     static constexpr int kLse = kPair + 3 * kPairSlot;  // [2][BM] float (log2 units)
     static constexpr int kDel = kLse + 2 * kBM * 4;     // [2][BM] float
-    static constexpr int kBar = kDel + 2 * kBM * 4;
+    static constexpr int kZero = kDel + 2 * kBM * 4;    // 4 KB of zeros (per-head dpair fill)
+    static constexpr int kZeroBytes = 4096;
+    static constexpr int kBar = kZero + kZeroBytes;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kTotal = kTmemSlot + 16;
     static constexpr int kAlloc = kTotal + 1024;
@@ -177,8 +180,12 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 const int h = kvh * p.n_rep + t / nq;
                 const int q0 = (qt0 + t % nq) * kBM;
                 mbar_expect_tx(&bars[kPairFull + slot], Lay::kPairSlot);
-                tma_load_4d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot], hf * kHM,
-                            (int)k0, q0 / kBM, b * QH + h);
+                if (p.pair_per_head)   // [B·H][KL][QL]
+                    tma_load_3d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot],
+                                q0 + hf * kHM, (int)k0, b * QH + h);
+                else                   // per-head tiles [B·H][QLp/128][KLp][128]
+                    tma_load_4d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot],
+                                hf * kHM, (int)k0, q0 / kBM, b * QH + h);
                 pair_issued = n + 1;
                 return true;
             };
@@ -241,8 +248,11 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     // store issued two halves ago must have read its source.
                     const int h = kvh * p.n_rep + t / nq;
                     const int q0 = (qt0 + t % nq) * kBM;
-                    tma_store_4d(&tm_ds, smem + Lay::kDS + s * Lay::kDSBytes + hf * kBN * 128, hf * kHM, (int)k0,
-                                 q0 / kBM, b * QH + h);
+                    const uint8_t* src = smem + Lay::kDS + s * Lay::kDSBytes + hf * kBN * 128;
+                    if (p.pair_per_head)   // straight into dpair [B·H][KL][QL] (clipped at QL, KL)
+                        tma_store_3d(&tm_ds, src, q0 + hf * kHM, (int)k0, b * QH + h);
+                    else
+                        tma_store_4d(&tm_ds, src, hf * kHM, (int)k0, q0 / kBM, b * QH + h);
                     bulk_commit();
                     bulk_wait_read<2>();
                 }
@@ -406,6 +416,37 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         // are clipped by the tensor map)
         const int w = warp & 3;
         const uint32_t lane_off = (uint32_t)(w * 32) << 16;
+        // A per-head dpair gets its zeros here, before the first dQ tile: this
+        // CTA's key rows, queries [0, i_lo) of every head of the group -- the
+        // part no tile covers (above the causal diagonal; all of it past the
+        // last kept key).  Bulk copies from a zeroed 4 KB buffer, in flight
+        // while the tiles run; under the causal mask the CTAs with the most
+        // zeros (late key tiles) are the ones with the fewest tiles.
+        int64_t i_lo = 0;
+        if (PAIR && p.pair_per_head) i_lo = nq == 0 ? QL : (CAUSAL ? (k0 < QL ? k0 : QL) : 0);
+        if (w == 0 && i_lo > 0) {
+            uint8_t* zb = smem + Lay::kZero;
+            for (int u = lane; u < Lay::kZeroBytes / 16; u += 32)
+                reinterpret_cast<uint4*>(zb)[u] = make_uint4(0u, 0u, 0u, 0u);
+            fence_proxy_async_smem();   // generic zero writes -> bulk-copy (async proxy) reads
+            __syncwarp();
+            // lane 1: its own bulk groups, apart from lane 0's reduce-adds
+            if (lane == 1) {
+                const int64_t rows = KL - k0 < kBN ? KL - k0 : kBN;
+                const int64_t row_bytes = i_lo * 2;
+                for (int r = 0; r < p.n_rep; ++r) {
+                    uint8_t* base = reinterpret_cast<uint8_t*>(p.dpair) +
+                                    (((int64_t)b * QH + kvh * p.n_rep + r) * KL + k0) * QL * 2;
+                    for (int64_t jr = 0; jr < rows; ++jr)
+                        for (int64_t off = 0; off < row_bytes; off += Lay::kZeroBytes) {
+                            const int64_t n = row_bytes - off < Lay::kZeroBytes ? row_bytes - off : Lay::kZeroBytes;
+                            bulk_store(base + jr * QL * 2 + off, zb, (uint32_t)n);
+                        }
+                }
+                bulk_commit();
+            }
+            __syncwarp();
+        }
         for (int t = 0; t < tiles; ++t) {
             const int h = kvh * p.n_rep + t / nq;
             const int q0 = (qt0 + t % nq) * kBM;
@@ -440,7 +481,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             }
             __syncwarp();
         }
-        if (lane == 0) bulk_wait<0>();   // reductions land before the CTA exits
+        if (lane == 0 || (lane == 1 && w == 0 && i_lo > 0)) bulk_wait<0>();   // reductions, zeros land before exit
     }
     tc_fence_before();
     __syncthreads();
@@ -477,8 +518,12 @@ int launch(const Params& p, const void* pair_tiles, void* ds_tiles, cudaStream_t
         !make_map(&tv, p.v, kE, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tdo, p.dO, kE, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_dq_map(&tdq, p.dq_acc, p.QL, (int64_t)p.B * p.QH) ||
-        (PAIR && (!make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16) ||
-                  !make_tiles_map(&tds, ds_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16))))
+        (PAIR && !p.pair_per_head &&
+         (!make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16) ||
+          !make_tiles_map(&tds, ds_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16))) ||
+        (PAIR && p.pair_per_head &&
+         (!make_per_head_map(&tp, p.pair, p.QL, p.KL, (int64_t)p.B * p.QH, bf16) ||
+          !make_per_head_map(&tds, p.dpair, p.QL, p.KL, (int64_t)p.B * p.QH, bf16))))
         return fail(NNOP_ERR_CUDA, "flash_attention_bwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_bwd_sm100_kernel<T, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)

@@ -35,6 +35,10 @@ struct Params {
     int64_t QL, KL;
     int E, QH, KH, B, n_rep;
     float scale;
+    // pair / dpair laid out per head, [B][QH][KL][QL] (Julia (QL, KL, H, B)),
+    // read and written by the tcgen05 kernels directly; 0: the reference's
+    // head-innermost layout, which reaches them as per-head tiles (pair_tiles.cu)
+    int pair_per_head;
 };
 
 // Index of the last kept key + 1 for one batch row of the key-padding mask

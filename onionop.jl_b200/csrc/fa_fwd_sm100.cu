@@ -191,9 +191,13 @@ fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     return false;
                 mbar_expect_tx(&bars[kPairFull + slot], L::kPairBytes);
 #pragma unroll
-                for (int half = 0; half < 2; ++half)
-                    tma_load_4d(smem + L::kPair + slot * L::kPairBytes + half * kBN * 128, &tm_pair,
-                                &bars[kPairFull + slot], half * 64, j * kBN, qt, bh_q);
+                for (int half = 0; half < 2; ++half) {
+                    uint8_t* dst = smem + L::kPair + slot * L::kPairBytes + half * kBN * 128;
+                    if (p.pair_per_head)   // [B·H][KL][QL]: queries qt·128 + half·64.., keys j·128..
+                        tma_load_3d(dst, &tm_pair, &bars[kPairFull + slot], qt * kBM + half * 64, j * kBN, bh_q);
+                    else                   // per-head tiles [B·H][QLp/128][KLp][128]
+                        tma_load_4d(dst, &tm_pair, &bars[kPairFull + slot], half * 64, j * kBN, qt, bh_q);
+                }
                 pair_issued = j + 1;
                 return true;
             };
@@ -433,7 +437,8 @@ int launch(const Params& p, const void* pair_tiles, cudaStream_t s) {
     if (!make_map(&tq, p.q, E, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
         !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
-        (PAIR && !make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16)))
+        (PAIR && !(p.pair_per_head ? make_per_head_map(&tp, p.pair, p.QL, p.KL, (int64_t)p.B * p.QH, bf16)
+                                   : make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16))))
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cuTensorMapEncodeTiled failed");
     auto kern = fa_fwd_sm100_kernel<T, E, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)

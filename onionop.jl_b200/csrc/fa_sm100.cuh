@@ -162,6 +162,25 @@ bool make_tiles_map(CUtensorMap* m, const void* base, int64_t qlp, int64_t klp, 
     return r == CUDA_SUCCESS;
 }
 
+// 3-D map over a pair bias laid out per head, [B·H][KL][QL] 16-bit (Julia
+// (QL, KL, H, B)), box (64 queries, 128 keys, 1), 128-byte swizzle: the same
+// [key][64 queries] half tile the per-head tiles map yields, read (or, for
+// dpair, written) in place.  Rows past KL / columns past QL are zero-filled
+// on loads and clipped on stores.  The row stride QL·2 bytes must be a
+// multiple of 16 (QL % 8 == 0).
+bool make_per_head_map(CUtensorMap* m, const void* base, int64_t QL, int64_t KL, int64_t bh, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)QL, (cuuint64_t)KL, (cuuint64_t)bh};
+    cuuint64_t strides[2] = {(cuuint64_t)QL * 2, (cuuint64_t)QL * KL * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace
 }  // namespace fa
 }  // namespace nnop

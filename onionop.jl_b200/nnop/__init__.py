@@ -30,6 +30,7 @@ from ._lib import (BF16, F16, F32, NNopError, NNopShapeError, check, lib)
 
 __all__ = [
     "flash_attention", "_flash_attention", "grad_flash_attention",
+    "flash_attention_pair_per_head", "_flash_attention_pair_per_head", "grad_flash_attention_pair_per_head",
     "online_softmax", "grad_online_softmax",
     "rms_norm", "_rms_norm", "grad_rms_norm",
     "layer_norm", "_layer_norm", "grad_layer_norm",
@@ -187,6 +188,89 @@ def flash_attention(q, k, v, pair=None, *, causal: bool, kpad_mask=None):
     if any(within_gradient(t) for t in (q, k, v, pair)):
         return _FlashAttentionFn.apply(q, k, v, pair, kpad_mask, bool(causal))
     return _flash_attention(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)[0]
+
+
+# -------------------------------------------------------------------------
+# pair bias laid out per head: Julia (QL, KL, QH, B) = torch (B, QH, KL, QL)
+# -------------------------------------------------------------------------
+
+def _per_head_dims(q, k, v, pair, kpad_mask):
+    if pair is None:
+        raise NNopError(-3, "the per-head entry points take a pair bias")
+    if pair.dim() != 4:
+        raise NNopShapeError(-1, "pair must be 4-d (B, QH, KL, QL)")
+    B, QH, QL, E, KH, KL = _fa_dims(q, k, v, None, kpad_mask)
+    if tuple(pair.shape) != (B, QH, KL, QL):
+        raise NNopShapeError(-1, f"pair must have shape (B, QH, KL, QL) = {(B, QH, KL, QL)}, got {tuple(pair.shape)}")
+    if pair.dtype != q.dtype:
+        raise NNopError(-2, "pair must have the dtype of q")
+    return B, QH, QL, E, KH, KL
+
+
+def _flash_attention_pair_per_head(q, k, v, pair, *, causal: bool, kpad_mask=None):
+    """``_flash_attention`` with the pair bias laid out per head, torch shape
+    (B, QH, KL, QL) (Julia (QL, KL, QH, B)), read in place by the tensor-core
+    kernel (no re-layout pass, no workspace).  bf16/f16, E = 64, QL % 8 == 0;
+    −Inf bias entries only at keys ``kpad_mask`` removes.  Returns ``(o, lse)``."""
+    dev = _dev(q, k, v, pair, kpad_mask)
+    B, QH, QL, E, KH, KL = _per_head_dims(q, k, v, pair, kpad_mask)
+    q, k, v, pair = _contig(q), _contig(k), _contig(v), _contig(pair)
+    m = _mask_u8(kpad_mask)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, QH, QL), dtype=torch.float32, device=dev)
+    check(lib.nnop_flash_attention_fwd_pair_per_head(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m), _ptr(o), _ptr(lse),
+        E, QL, KL, QH, KH, B, int(bool(causal)), _dtype_id(q), _stream(dev)))
+    return o, lse
+
+
+def grad_flash_attention_pair_per_head(do, o, lse, q, k, v, pair, *, causal: bool, kpad_mask=None):
+    """``∇flash_attention`` with pair and dpair laid out per head (B, QH, KL, QL):
+    returns ``(dq, dk, dv, dpair)``; dS is stored straight into dpair."""
+    dev = _dev(do, o, lse, q, k, v, pair, kpad_mask)
+    B, QH, QL, E, KH, KL = _per_head_dims(q, k, v, pair, kpad_mask)
+    do, o, q, k, v, pair = map(_contig, (do, o, q, k, v, pair))
+    if do.dtype != q.dtype:
+        do = do.to(q.dtype)
+    lse = lse.contiguous()
+    m = _mask_u8(kpad_mask)
+    dq, dk, dv, dpair = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(pair)
+    dt = _dtype_id(q)
+    ws_bytes = lib.nnop_flash_attention_bwd_pair_per_head_workspace_size(E, QL, KL, QH, KH, B, dt)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    check(lib.nnop_flash_attention_bwd_pair_per_head(
+        _ptr(do), _ptr(o), _ptr(lse), _ptr(q), _ptr(k), _ptr(v), _ptr(pair), _ptr(m),
+        _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dpair), _ptr(ws), ws_bytes,
+        E, QL, KL, QH, KH, B, int(bool(causal)), dt, _stream(dev)))
+    return dq, dk, dv, dpair
+
+
+class _FlashAttentionPerHeadFn(torch.autograd.Function):
+    """The rrule of ``flash_attention_pair_per_head`` (the structure of
+    src/attention_crc.jl:16-31 with the per-head pair layout)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, pair, kpad_mask, causal):
+        o, lse = _flash_attention_pair_per_head(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)
+        ctx.save_for_backward(o, lse, q, k, v, pair, kpad_mask)
+        ctx.causal = causal
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        o, lse, q, k, v, pair, kpad_mask = ctx.saved_tensors
+        dq, dk, dv, dpair = grad_flash_attention_pair_per_head(do, o, lse, q, k, v, pair, causal=ctx.causal,
+                                                               kpad_mask=kpad_mask)
+        return dq, dk, dv, dpair, None, None
+
+
+def flash_attention_pair_per_head(q, k, v, pair, *, causal: bool, kpad_mask=None):
+    """``flash_attention`` with the pair bias laid out per head, torch shape
+    (B, QH, KL, QL) (Julia (QL, KL, QH, B)); differentiable w.r.t. q, k, v,
+    pair.  Same results as ``flash_attention(q, k, v, pair.permute(0, 2, 3, 1))``."""
+    if any(within_gradient(t) for t in (q, k, v, pair)):
+        return _FlashAttentionPerHeadFn.apply(q, k, v, pair, kpad_mask, bool(causal))
+    return _flash_attention_pair_per_head(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)[0]
 
 
 # =========================================================================

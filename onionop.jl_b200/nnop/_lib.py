@@ -41,6 +41,12 @@ SIGNATURES = {
                                               _vp, _sz, _vp, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int,
                                               _vp]),
     "nnop_flash_attention_bwd_workspace_size_reuse": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int, _sz, _int]),
+    "nnop_flash_attention_fwd_pair_per_head": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                      _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
+    "nnop_flash_attention_bwd_pair_per_head_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
+    "nnop_flash_attention_bwd_pair_per_head": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                      _vp, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int,
+                                                      _vp]),
     "nnop_online_softmax_fwd": (_int, [_vp, _vp, _i64, _i64, _int, _vp]),
     "nnop_online_softmax_bwd": (_int, [_vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "nnop_rms_norm_fwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f, _f, _int, _vp]),
