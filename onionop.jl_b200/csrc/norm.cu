@@ -728,6 +728,22 @@ int check_norm_args(int64_t emb, int64_t n) {
 }
 
 }  // namespace
+
+// The shared-memory ring kernels (norm_ring.cu): launched when they apply.
+namespace ring {
+template <typename T>
+bool rms_fwd(const T* x, const T* w, T* y, float* rstd, int emb, int64_t n, float eps, float offset, cudaStream_t s,
+             int* st);
+template <typename T>
+bool rms_bwd(const T* dy, const T* x, const T* w, const float* rstd, T* dx, float* partial, int emb, int64_t n,
+             float offset, int max_parts, cudaStream_t s, int* parts, int* st);
+template <typename T>
+bool ln_fwd(const T* x, const T* w, const T* b, T* y, float* mean, float* rstd, int emb, int64_t n, float eps,
+            cudaStream_t s, int* st);
+template <typename T>
+bool ln_bwd(const T* dy, const T* x, const T* w, const float* mean, const float* rstd, T* dx, float* partial,
+            int emb, int64_t n, int max_parts, cudaStream_t s, int* parts, int* st);
+}  // namespace ring
 }  // namespace nnop
 
 using namespace nnop;
@@ -742,6 +758,8 @@ int nnop_rms_norm_fwd(const void* x, const void* w, void* y, float* rstd, int64_
     if (!x || !w || !y || !rstd) return fail(NNOP_ERR_ARG, "rms_norm_fwd: NULL pointer");
     cudaStream_t s = (cudaStream_t)stream;
     NNOP_DISPATCH_DTYPE(dtype, T, {
+        int rst = NNOP_OK;
+        if (ring::rms_fwd<T>((const T*)x, (const T*)w, (T*)y, rstd, (int)emb, n, eps, offset, s, &rst)) return rst;
         RowPlan p = plan_rows<T>((int)emb, {x, w, y});
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
@@ -774,17 +792,20 @@ int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w, const float*
     float* partial = (float*)workspace;
     int parts = 0;
     NNOP_DISPATCH_DTYPE(dtype, T, {
-        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
-        NNOP_VEC_SWITCH(p.vec, T, VC, {
-            NNOP_NV_SWITCH(p.nv, NVC, {
-                auto kern = rms_bwd_kernel<T, VC, NVC>;
-                parts = bwd_grid(kern, p.block, n);
-                kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, rstd, (T*)dx,
-                                                partial, (int)emb, n, offset, 1.0f / (float)emb);
+        if (!ring::rms_bwd<T>((const T*)dy, (const T*)x, (const T*)w, rstd, (T*)dx, partial, (int)emb, n, offset,
+                              (int)bwd_max_parts(n), s, &parts, &st)) {
+            RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
+            NNOP_VEC_SWITCH(p.vec, T, VC, {
+                NNOP_NV_SWITCH(p.nv, NVC, {
+                    auto kern = rms_bwd_kernel<T, VC, NVC>;
+                    parts = bwd_grid(kern, p.block, n);
+                    kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, rstd, (T*)dx,
+                                                    partial, (int)emb, n, offset, 1.0f / (float)emb);
+                });
             });
-        });
+            st = check_launch("rms_norm_bwd");
+        }
     });
-    st = check_launch("rms_norm_bwd");
     if (st) return st;
     reduce_partials_kernel<float><<<(unsigned)((emb + 255) / 256), 256, 0, s>>>(partial, dw, (int)emb, emb, parts);
     return check_launch("rms_norm_bwd reduce");
@@ -798,6 +819,9 @@ int nnop_layer_norm_fwd(const void* x, const void* w, const void* b, void* y, fl
     if (!x || !w || !b || !y || !mean || !rstd) return fail(NNOP_ERR_ARG, "layer_norm_fwd: NULL pointer");
     cudaStream_t s = (cudaStream_t)stream;
     NNOP_DISPATCH_DTYPE(dtype, T, {
+        int rst = NNOP_OK;
+        if (ring::ln_fwd<T>((const T*)x, (const T*)w, (const T*)b, (T*)y, mean, rstd, (int)emb, n, eps, s, &rst))
+            return rst;
         RowPlan p = plan_rows<T>((int)emb, {x, w, b, y});
         NNOP_VEC_SWITCH(p.vec, T, VC, {
             NNOP_NV_SWITCH(p.nv, NVC, {
@@ -834,16 +858,19 @@ int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w, const floa
     float* partial = (float*)workspace;
     int parts = 0;
     NNOP_DISPATCH_DTYPE(dtype, T, {
-        RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
-        NNOP_VEC_SWITCH(p.vec, T, VC, {
-            NNOP_NV_SWITCH(p.nv, NVC, {
-                auto kern = ln_bwd_kernel<T, VC, NVC>;
-                parts = bwd_grid(kern, p.block, n);
-                kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, mean, rstd,
-                                                (T*)dx, partial, (int)emb, n, 1.0f / (float)emb);
+        if (!ring::ln_bwd<T>((const T*)dy, (const T*)x, (const T*)w, mean, rstd, (T*)dx, partial, (int)emb, n,
+                             (int)bwd_max_parts(n), s, &parts, &st)) {
+            RowPlan p = plan_rows<T>((int)emb, {dy, x, w, dx}, 32);
+            NNOP_VEC_SWITCH(p.vec, T, VC, {
+                NNOP_NV_SWITCH(p.nv, NVC, {
+                    auto kern = ln_bwd_kernel<T, VC, NVC>;
+                    parts = bwd_grid(kern, p.block, n);
+                    kern<<<parts, p.block, 0, s>>>((const T*)dy, (const T*)x, (const T*)w, mean, rstd,
+                                                    (T*)dx, partial, (int)emb, n, 1.0f / (float)emb);
+                });
             });
-        });
-        st = check_launch("layer_norm_bwd");
+            st = check_launch("layer_norm_bwd");
+        }
         if (st) return st;
         const unsigned g = (unsigned)((emb + 255) / 256);
         reduce_partials_kernel<T><<<g, 256, 0, s>>>(partial, (T*)dw, (int)emb, 2 * emb, parts);
