@@ -224,6 +224,45 @@ int nnop_flash_attention_bwd_pair_per_head(const void* dO, const void* o, const 
                                            int64_t QH, int64_t KH, int64_t B,
                                            int causal, int dtype, void* stream);
 
+/*
+ * Llama RoPE fused with attention, forward.  No single counterpart in the
+ * reference: the composition `flash_attention(llama_rope(q, k; cos, sin)...)`
+ * of `llama_rope` (src/rope/llama_rope.jl:69-98) and `_flash_attention`
+ * (src/attention.jl:145-197).  Rotates q and k (written to q_rot, k_rot --
+ * the backward's inputs) and runs the attention forward on them.
+ *   q [B][QH][L][E], k, v [B][KH][L][E]; cos, sin [cos_batch][L][E] f32
+ *   (cos_batch = 1 or B); o, lse as nnop_flash_attention_fwd.
+ *   bf16 / f16, E = 64 or 128, no pair bias.
+ */
+int nnop_flash_attention_rope_fwd(const void* q, const void* k, const void* v,
+                                  const float* cos_t, const float* sin_t,
+                                  const uint8_t* kpad_mask, void* q_rot, void* k_rot,
+                                  void* o, float* lse,
+                                  int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                                  int64_t cos_batch, int causal, int dtype, void* stream);
+
+/* Bytes of workspace nnop_flash_attention_rope_bwd needs. */
+size_t nnop_flash_attention_rope_bwd_workspace_size(int64_t E, int64_t L, int64_t QH,
+                                                    int64_t KH, int64_t B, int dtype);
+
+/*
+ * Backward of the fused RoPE attention: the composition of `∇flash_attention`
+ * (src/attention_bwd.jl:213-303) and `∇llama_rope` (src/rope/llama_rope.jl:86-92)
+ * with the inverse rotation folded into the attention backward's outputs (dq
+ * while its fp32 accumulator is converted, dk in the kernel's dK epilogue):
+ * dq, dk are the gradients of the UN-rotated q and k; dv as usual.
+ *   q_rot, k_rot, o, lse from nnop_flash_attention_rope_fwd.
+ *   workspace: >= nnop_flash_attention_rope_bwd_workspace_size(...) bytes,
+ *   256-byte aligned.
+ */
+int nnop_flash_attention_rope_bwd(const void* dO, const void* o, const float* lse,
+                                  const void* q_rot, const void* k_rot, const void* v,
+                                  const float* cos_t, const float* sin_t,
+                                  const uint8_t* kpad_mask, void* dq, void* dk, void* dv,
+                                  void* workspace, size_t workspace_bytes,
+                                  int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                                  int64_t cos_batch, int causal, int dtype, void* stream);
+
 /* --------------------------------------------------------------------------
  * Online softmax over the contiguous axis (Julia dims=1)
  * -------------------------------------------------------------------------- */
@@ -270,6 +309,36 @@ int nnop_rms_norm_bwd(const void* dy, const void* x, const void* w,
                       void* workspace, size_t workspace_bytes,
                       int64_t emb, int64_t n, float offset,
                       int dtype, void* stream);
+
+/*
+ * Residual add fused into RMSNorm.  No counterpart in the reference's API: it
+ * is the composition a transformer block performs around `rms_norm`
+ * (src/rms_norm.jl:117-137), h = x + residual then rms_norm(h), in one pass
+ * over x and residual instead of an add pass and a norm pass that reads h
+ * back.
+ *   x, residual, h, y [n][emb] dtype; w [emb]; rstd [n] f32.
+ *   h = x + residual (rounded to dtype, the values a separate add stores);
+ *   y = (offset + w)·h·rstd, rstd = 1/sqrt(mean(h²) + eps).
+ */
+int nnop_add_rms_norm_fwd(const void* x, const void* residual, const void* w,
+                          void* h, void* y, float* rstd,
+                          int64_t emb, int64_t n, float eps, float offset,
+                          int dtype, void* stream);
+
+size_t nnop_add_rms_norm_bwd_workspace_size(int64_t emb, int64_t n);
+
+/*
+ * Backward of the fused residual add + RMSNorm.
+ *   dy [n][emb]: gradient of y; dh [n][emb] or NULL: the gradient reaching h
+ *   from its other use (the residual stream); h, rstd from the forward.
+ *   dx = ∇rms_norm(dy, h) + dh -- the gradient of both x and residual; dw f32.
+ *   workspace: >= nnop_add_rms_norm_bwd_workspace_size(emb, n) bytes.
+ */
+int nnop_add_rms_norm_bwd(const void* dy, const void* dh, const void* h,
+                          const void* w, const float* rstd, void* dx, float* dw,
+                          void* workspace, size_t workspace_bytes,
+                          int64_t emb, int64_t n, float offset,
+                          int dtype, void* stream);
 
 /*
  * RMSNorm backward that allocates nothing.  No counterpart in the reference.

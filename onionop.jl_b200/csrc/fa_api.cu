@@ -531,3 +531,112 @@ int nnop_flash_attention_bwd_pair_per_head(const void* dO, const void* o, const 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Llama RoPE fused with attention.
+//
+// The reference composes `llama_rope` (src/rope/llama_rope.jl:69-98) with
+// `flash_attention` (src/attention_crc.jl:4-31): two passes forward (rotate,
+// attend) and two backward (attention backward, then the inverse rotation of
+// dq and dk).  These entry points keep the forward's rotation as one launch
+// (its rotated q and k are the attention backward's inputs, returned to the
+// caller to save) and fold the backward's inverse rotation into the
+// attention backward's own outputs: dq is rotated while its fp32 accumulator
+// is converted to the dtype, dk in the tensor-core kernel's dK epilogue --
+// the separate RoPE backward pass (a read and a write of dq and dk) is gone.
+// bf16 / f16, E = 64 or 128, no pair bias, q and k of one sequence length L;
+// cos, sin [cos_batch][L][E] fp32 with cos_batch = 1 or B.
+// ---------------------------------------------------------------------------
+namespace nnop {
+namespace {
+
+int check_rope_attention(const char* what, int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                         int64_t cos_batch, int dtype) {
+    int st = check_dims(E, L, L, QH, KH, B, dtype);
+    if (st) return st;
+    if (dtype != NNOP_BF16 && dtype != NNOP_F16)
+        return fail(NNOP_ERR_DTYPE, std::string(what) + ": fused RoPE attention takes bf16 or f16");
+    if (E != 64 && E != 128)
+        return fail(NNOP_ERR_SHAPE, std::string(what) + ": fused RoPE attention takes E = 64 or 128");
+    if (cos_batch != 1 && cos_batch != B)
+        return fail(NNOP_ERR_SHAPE, std::string(what) + ": cos/sin batch must equal the q/k batch or be 1");
+    if ((L + 31) / 32 > 2048) return fail(NNOP_ERR_SHAPE, std::string(what) + ": sequence longer than 65536");
+    return NNOP_OK;
+}
+
+}  // namespace
+}  // namespace nnop
+
+extern "C" {
+
+int nnop_flash_attention_rope_fwd(const void* q, const void* k, const void* v, const float* cos_t,
+                                  const float* sin_t, const uint8_t* kpad_mask, void* q_rot, void* k_rot, void* o,
+                                  float* lse, int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                                  int64_t cos_batch, int causal, int dtype, void* stream) {
+    int st = check_rope_attention("flash_attention_rope_fwd", E, L, QH, KH, B, cos_batch, dtype);
+    if (st) return st;
+    if (L == 0 || B == 0) return NNOP_OK;
+    if ((st = nnop_llama_rope(q, k, cos_t, sin_t, q_rot, k_rot, E, L, QH, KH, B, cos_batch, 1.0f, dtype, stream)))
+        return st;
+    return nnop_flash_attention_fwd(q_rot, k_rot, v, nullptr, kpad_mask, o, lse, nullptr, 0, E, L, L, QH, KH, B, causal,
+                                    dtype, stream);
+}
+
+size_t nnop_flash_attention_rope_bwd_workspace_size(int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                                                    int dtype) {
+    (void)KH;
+    if (E <= 0 || L < 0 || QH <= 0 || B < 0) return 0;
+    return bwd_layout(nullptr, E, L, L, QH, B, false, false, dtype).bytes;
+}
+
+int nnop_flash_attention_rope_bwd(const void* dO, const void* o, const float* lse, const void* q_rot,
+                                  const void* k_rot, const void* v, const float* cos_t, const float* sin_t,
+                                  const uint8_t* kpad_mask, void* dq, void* dk, void* dv, void* workspace,
+                                  size_t workspace_bytes, int64_t E, int64_t L, int64_t QH, int64_t KH, int64_t B,
+                                  int64_t cos_batch, int causal, int dtype, void* stream) {
+    int st = check_rope_attention("flash_attention_rope_bwd", E, L, QH, KH, B, cos_batch, dtype);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (L == 0 || B == 0) return NNOP_OK;
+    if (!dO || !o || !lse || !q_rot || !k_rot || !v || !cos_t || !sin_t || !dq || !dk || !dv)
+        return fail(NNOP_ERR_ARG, "flash_attention_rope_bwd: NULL pointer");
+    if (!aligned16(dO) || !aligned16(o) || !aligned16(q_rot) || !aligned16(k_rot) || !aligned16(v) ||
+        !aligned16(dq) || !aligned16(dk) || !aligned16(dv) || !aligned16(cos_t) || !aligned16(sin_t))
+        return fail(NNOP_ERR_ALIGN, "flash_attention_rope_bwd: tensors must be 16-byte aligned");
+    BwdWorkspace ws = bwd_layout(workspace, E, L, L, QH, B, false, false, dtype);
+    if (!workspace || workspace_bytes < ws.bytes)
+        return fail(NNOP_ERR_WORKSPACE, "flash_attention_rope_bwd: workspace too small (need " +
+                                            std::to_string(ws.bytes) + " bytes)");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return fail(NNOP_ERR_ALIGN, "flash_attention_rope_bwd: workspace must be 256-byte aligned");
+    fa::Params p{};
+    p.q = q_rot; p.k = k_rot; p.v = v; p.kmask = kpad_mask; p.o = const_cast<void*>(o);
+    p.lse = const_cast<float*>(lse); p.dO = dO;
+    p.dq = dq; p.dk = dk; p.dv = dv;
+    p.QL = L; p.KL = L; p.E = (int)E; p.QH = (int)QH; p.KH = (int)KH; p.B = (int)B;
+    p.n_rep = (int)(QH / KH);
+    p.delta = ws.delta;
+    p.kv_len = kpad_mask ? ws.kv_len : nullptr;
+    p.dq_acc = ws.dq_acc;
+    p.rope_cos = cos_t; p.rope_sin = sin_t; p.rope_cb = cos_batch;
+    const float sc = (float)(1.0 / sqrt((double)E));
+    p.scale = dtype == NNOP_BF16 ? __bfloat162float(__float2bfloat16_rn(sc)) : __half2float(__float2half_rn(sc));
+    const int64_t rows = B * QH * L;
+    if (kpad_mask && (st = fa_host::launch_kv_len(kpad_mask, ws.kv_len, L, (int)B, s))) return st;
+    if (cudaMemsetAsync(ws.dq_acc, 0, (size_t)rows * E * sizeof(float), s) != cudaSuccess)
+        return fail(NNOP_ERR_CUDA, "flash_attention_rope_bwd: memset failed");
+    const bool c = causal != 0;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        if constexpr (sizeof(T) == 2) {
+            if ((st = fa_host::launch_preprocess<T>((const T*)dO, (const T*)o, ws.delta, rows, (int)E, s))) return st;
+            const int slot = timer_begin(1, s);
+            st = fa::sm100_bwd(p, nullptr, nullptr, dtype, c, s);
+            timer_end(1, slot, s);
+            if (st) return st;
+            return fa_host::launch_convert_rope<T>(ws.dq_acc, (T*)dq, cos_t, sin_t, cos_batch, B, QH, L, (int)E, s);
+        }
+    });
+    return fail(NNOP_ERR_DTYPE, "flash_attention_rope_bwd: bf16 or f16 only");
+}
+
+}  // extern "C"

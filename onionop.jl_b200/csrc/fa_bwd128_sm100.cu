@@ -346,21 +346,60 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
             const uint32_t src = (is_dk ? tDK : tDV) + lane_off;
             T* dst = reinterpret_cast<T*>(is_dk ? p.dk : p.dv) + (((int64_t)b * p.KH + kvh) * KL + j) * kE;
             const float mul = is_dk ? p.scale : 1.f;
+            if (is_dk && p.rope_cos != nullptr) {
+                // fused RoPE backward: dk of the un-rotated k, pairs (e, e + 64)
+                // rotated by cos/sin of index e at position j (sin → −sin)
+                const int64_t tr = ((p.rope_cb == 1 ? 0 : (int64_t)b) * KL + (j < KL ? j : 0)) * kE;
 #pragma unroll 1
-            for (int c = 0; c < kE / 32; ++c) {
-                uint32_t raw[32];
-                tmem_ld32(src + c * 32, raw);
-                tmem_ld_wait();
-                if (j < KL) {
-                    uint32_t pk[16];
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t ra[32], rb[32];
+                    tmem_ld32(src + c * 32, ra);
+                    tmem_ld32(src + 64 + c * 32, rb);
+                    tmem_ld_wait();
+                    if (j < KL) {
+                        uint32_t pa[16], pb[16];
 #pragma unroll
-                    for (int u = 0; u < 16; ++u)
-                        pk[u] = steps > 0 ? pack16<T>(__uint_as_float(raw[2 * u]) * mul,
-                                                      __uint_as_float(raw[2 * u + 1]) * mul)
-                                          : 0u;
-                    uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+                        for (int u = 0; u < 32; u += 2) {
+                            float oa[2], ob[2];
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) d4[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                            for (int v = 0; v < 2; ++v) {
+                                const float a = steps > 0 ? __uint_as_float(ra[u + v]) * mul : 0.f;
+                                const float bb = steps > 0 ? __uint_as_float(rb[u + v]) * mul : 0.f;
+                                const float cs = __ldg(p.rope_cos + tr + 32 * c + u + v);
+                                const float sn = __ldg(p.rope_sin + tr + 32 * c + u + v);
+                                oa[v] = a * cs + bb * sn;
+                                ob[v] = bb * cs - a * sn;
+                            }
+                            pa[u >> 1] = pack16<T>(oa[0], oa[1]);
+                            pb[u >> 1] = pack16<T>(ob[0], ob[1]);
+                        }
+                        uint4* da = reinterpret_cast<uint4*>(dst + c * 32);
+                        uint4* db = reinterpret_cast<uint4*>(dst + 64 + c * 32);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            da[v] = make_uint4(pa[4 * v], pa[4 * v + 1], pa[4 * v + 2], pa[4 * v + 3]);
+                            db[v] = make_uint4(pb[4 * v], pb[4 * v + 1], pb[4 * v + 2], pb[4 * v + 3]);
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kE / 32; ++c) {
+                    uint32_t raw[32];
+                    tmem_ld32(src + c * 32, raw);
+                    tmem_ld_wait();
+                    if (j < KL) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int u = 0; u < 16; ++u)
+                            pk[u] = steps > 0 ? pack16<T>(__uint_as_float(raw[2 * u]) * mul,
+                                                          __uint_as_float(raw[2 * u + 1]) * mul)
+                                              : 0u;
+                        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v)
+                            d4[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                    }
                 }
             }
         }

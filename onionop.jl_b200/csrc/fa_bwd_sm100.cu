@@ -391,20 +391,58 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const uint32_t src = (is_dk ? tDK : tDV) + lane_off;
             T* dst = reinterpret_cast<T*>(is_dk ? p.dk : p.dv) + (((int64_t)b * p.KH + kvh) * KL + j) * kE;
             const float mul = is_dk ? p.scale : 1.f;
+            if (is_dk && p.rope_cos != nullptr) {
+                // fused RoPE backward: dk of the un-rotated k, pairs (e, e + 32)
+                // rotated by cos/sin of index e at position j (sin → −sin)
+                const int64_t tr = ((p.rope_cb == 1 ? 0 : (int64_t)b) * KL + (j < KL ? j : 0)) * kE;
+#pragma unroll 1
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t ra[16], rb[16];
+                    tmem_ld16(src + c * 16, ra);
+                    tmem_ld16(src + 32 + c * 16, rb);
+                    tmem_ld_wait();
+                    if (j < KL) {
+                        uint32_t pa[8], pb[8];
 #pragma unroll
-            for (int c = 0; c < kE / 16; ++c) {
-                uint32_t raw[16];
-                tmem_ld16(src + c * 16, raw);
-                tmem_ld_wait();
-                if (j < KL) {
-                    uint32_t pk[8];
+                        for (int u = 0; u < 16; u += 2) {
+                            float oa[2], ob[2];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        pk[u] = tiles > 0 ? pack16<T>(__uint_as_float(raw[2 * u]) * mul, __uint_as_float(raw[2 * u + 1]) * mul)
-                                          : 0u;
-                    uint4* d4 = reinterpret_cast<uint4*>(dst + c * 16);
-                    d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            for (int v = 0; v < 2; ++v) {
+                                const float a = tiles > 0 ? __uint_as_float(ra[u + v]) * mul : 0.f;
+                                const float bb = tiles > 0 ? __uint_as_float(rb[u + v]) * mul : 0.f;
+                                const float cs = __ldg(p.rope_cos + tr + 16 * c + u + v);
+                                const float sn = __ldg(p.rope_sin + tr + 16 * c + u + v);
+                                oa[v] = a * cs + bb * sn;
+                                ob[v] = bb * cs - a * sn;
+                            }
+                            pa[u >> 1] = pack16<T>(oa[0], oa[1]);
+                            pb[u >> 1] = pack16<T>(ob[0], ob[1]);
+                        }
+                        uint4* da = reinterpret_cast<uint4*>(dst + c * 16);
+                        uint4* db = reinterpret_cast<uint4*>(dst + 32 + c * 16);
+                        da[0] = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+                        da[1] = make_uint4(pa[4], pa[5], pa[6], pa[7]);
+                        db[0] = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+                        db[1] = make_uint4(pb[4], pb[5], pb[6], pb[7]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < kE / 16; ++c) {
+                    uint32_t raw[16];
+                    tmem_ld16(src + c * 16, raw);
+                    tmem_ld_wait();
+                    if (j < KL) {
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            pk[u] = tiles > 0 ? pack16<T>(__uint_as_float(raw[2 * u]) * mul,
+                                                          __uint_as_float(raw[2 * u + 1]) * mul)
+                                              : 0u;
+                        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 16);
+                        d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    }
                 }
             }
         }

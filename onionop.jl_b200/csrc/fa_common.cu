@@ -9,7 +9,8 @@
 //                   head-innermost and coalesced.  The reference zero-fills the
 //                   whole dpair first (`KA.zeros`, src/attention_bwd.jl:250-252);
 //                   here every element is written exactly once;
-// * convert       : fp32 dq accumulator -> dq dtype.
+// * convert       : fp32 dq accumulator -> dq dtype (convert_rope: with the
+//                   inverse RoPE rotation, for the fused RoPE backward).
 #include "fa_common.cuh"
 
 namespace nnop {
@@ -79,6 +80,38 @@ __global__ void convert_kernel(const float* __restrict__ src, T* __restrict__ ds
     }
 }
 
+// dq fp32 accumulator -> dq dtype with the inverse RoPE rotation (the fused
+// RoPE backward): for the pair (e, e + E/2) of row (b, h, i),
+//   dq[e] = a·cos + b·sin,   dq[e + E/2] = b·cos − a·sin,
+// a, b the accumulator values, cos/sin of index e at position i (the
+// reference's ∇llama_rope, src/rope/llama_rope.jl:86-92: sin → −sin).  One
+// thread per 4 consecutive e of the first half.
+template <typename T>
+__global__ void convert_rope_kernel(const float* __restrict__ src, T* __restrict__ dst, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, int64_t cb, int64_t QH, int64_t L, int E,
+                                    int64_t total) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= total) return;
+    const int half = E / 2, q4 = half / 4;
+    const int e = (int)(t % q4) * 4;
+    const int64_t row = t / q4;                  // (b, h, i)
+    const int64_t i = row % L, b = row / (L * QH);
+    const int64_t tr = ((cb == 1 ? 0 : b) * L + i) * E + e;
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + tr);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + tr);
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(src + row * E + e));
+    const float4 bb = __ldcs(reinterpret_cast<const float4*>(src + row * E + e + half));
+    T* d = dst + row * E + e;
+    d[0] = from_f<T>(a.x * c.x + bb.x * sn.x);
+    d[1] = from_f<T>(a.y * c.y + bb.y * sn.y);
+    d[2] = from_f<T>(a.z * c.z + bb.z * sn.z);
+    d[3] = from_f<T>(a.w * c.w + bb.w * sn.w);
+    d[half + 0] = from_f<T>(bb.x * c.x - a.x * sn.x);
+    d[half + 1] = from_f<T>(bb.y * c.y - a.y * sn.y);
+    d[half + 2] = from_f<T>(bb.z * c.z - a.z * sn.z);
+    d[half + 3] = from_f<T>(bb.w * c.w - a.w * sn.w);
+}
+
 }  // namespace
 
 namespace fa_host {
@@ -123,6 +156,20 @@ template int launch_dpair_fill<float>(float*, const int*, int64_t, int64_t, int,
 template int launch_dpair_fill<__half>(__half*, const int*, int64_t, int64_t, int, int, int, bool, cudaStream_t);
 template int launch_dpair_fill<__nv_bfloat16>(__nv_bfloat16*, const int*, int64_t, int64_t, int, int, int, bool,
                                               cudaStream_t);
+template <typename T>
+int launch_convert_rope(const float* src, T* dst, const float* cos_t, const float* sin_t, int64_t cb, int64_t B,
+                        int64_t QH, int64_t L, int E, cudaStream_t s) {
+    const int64_t total = B * QH * L * (E / 8);
+    if (total == 0) return NNOP_OK;
+    convert_rope_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, s>>>(src, dst, cos_t, sin_t, cb, QH, L, E,
+                                                                            total);
+    return check_launch("flash_attention_bwd dq convert (rope)");
+}
+
+template int launch_convert_rope<__half>(const float*, __half*, const float*, const float*, int64_t, int64_t,
+                                         int64_t, int64_t, int, cudaStream_t);
+template int launch_convert_rope<__nv_bfloat16>(const float*, __nv_bfloat16*, const float*, const float*, int64_t,
+                                                int64_t, int64_t, int64_t, int, cudaStream_t);
 template int launch_convert<__half>(const float*, __half*, int64_t, cudaStream_t);
 template int launch_convert<__nv_bfloat16>(const float*, __nv_bfloat16*, int64_t, cudaStream_t);
 

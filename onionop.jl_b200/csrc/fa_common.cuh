@@ -39,6 +39,14 @@ struct Params {
     // read and written by the tcgen05 kernels directly; 0: the reference's
     // head-innermost layout, which reaches them as per-head tiles (pair_tiles.cu)
     int pair_per_head;
+    // Llama RoPE folded into the backward's outputs (the fused RoPE entry
+    // points): when rope_cos is set, dq and dk leave the backward rotated by
+    // the inverse rotation (sin → −sin), i.e. as gradients of the un-rotated
+    // q and k.  Tables [rope_cb][L][E] fp32 (rope_cb = 1 or B), L = QL = KL;
+    // pairs (e, e + E/2) use the cos/sin of index e (src/rope/llama_rope.jl:45-61).
+    const float* rope_cos;
+    const float* rope_sin;
+    int64_t rope_cb;
 };
 
 // Index of the last kept key + 1 for one batch row of the key-padding mask
@@ -72,6 +80,9 @@ int launch_dpair_fill(T* dpair, const int* kv_len, int64_t QL, int64_t KL, int Q
                       bool causal, cudaStream_t s);
 template <typename T>
 int launch_convert(const float* src, T* dst, int64_t n, cudaStream_t s);
+template <typename T>
+int launch_convert_rope(const float* src, T* dst, const float* cos_t, const float* sin_t, int64_t cb, int64_t B,
+                        int64_t QH, int64_t L, int E, cudaStream_t s);
 }  // namespace fa_host
 
 }  // namespace nnop

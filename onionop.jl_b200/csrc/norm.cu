@@ -743,7 +743,30 @@ bool ln_fwd(const T* x, const T* w, const T* b, T* y, float* mean, float* rstd, 
 template <typename T>
 bool ln_bwd(const T* dy, const T* x, const T* w, const float* mean, const float* rstd, T* dx, float* partial,
             int emb, int64_t n, int max_parts, cudaStream_t s, int* parts, int* st);
+template <typename T>
+bool add_rms_fwd(const T* x, const T* res, const T* w, T* h, T* y, float* rstd, int emb, int64_t n, float eps,
+                 float offset, cudaStream_t s, int* st);
+template <typename T>
+bool rms_bwd_add(const T* dy, const T* dh, const T* x, const T* w, const float* rstd, T* dx, float* partial, int emb,
+                 int64_t n, float offset, int max_parts, cudaStream_t s, int* parts, int* st);
 }  // namespace ring
+
+namespace {
+// out = a + b elementwise, rounded to T (the fused entry points' fallback for
+// rows the ring kernels do not take)
+template <typename T>
+__global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ out, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = from_f<T>(to_f(a[i]) + to_f(b[i]));
+}
+template <typename T>
+int launch_add(const T* a, const T* b, T* out, int64_t n, cudaStream_t s) {
+    if (n == 0) return NNOP_OK;
+    const int64_t g = (n + 255) / 256;
+    add_kernel<T><<<(unsigned)(g < 65536 ? g : 65536), 256, 0, s>>>(a, b, out, n);
+    return check_launch("residual add");
+}
+}  // namespace
 }  // namespace nnop
 
 using namespace nnop;
@@ -877,6 +900,64 @@ int nnop_layer_norm_bwd(const void* dy, const void* x, const void* w, const floa
         reduce_partials_kernel<T><<<g, 256, 0, s>>>(partial + emb, (T*)db, (int)emb, 2 * emb, parts);
     });
     return check_launch("layer_norm_bwd reduce");
+}
+
+// ---------------------------------------------------------------------------
+// Residual add fused into RMSNorm (no counterpart in the reference's API; the
+// composition of a transformer block's residual add with `rms_norm`,
+// src/rms_norm.jl:117-169).
+// ---------------------------------------------------------------------------
+
+int nnop_add_rms_norm_fwd(const void* x, const void* residual, const void* w, void* h, void* y, float* rstd,
+                          int64_t emb, int64_t n, float eps, float offset, int dtype, void* stream) {
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (n == 0) return NNOP_OK;
+    if (!x || !residual || !w || !h || !y || !rstd) return fail(NNOP_ERR_ARG, "add_rms_norm_fwd: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        int rst = NNOP_OK;
+        if (ring::add_rms_fwd<T>((const T*)x, (const T*)residual, (const T*)w, (T*)h, (T*)y, rstd, (int)emb, n, eps,
+                                 offset, s, &rst))
+            return rst;
+        if ((st = launch_add<T>((const T*)x, (const T*)residual, (T*)h, emb * n, s))) return st;
+    });
+    return nnop_rms_norm_fwd(h, w, y, rstd, emb, n, eps, offset, dtype, stream);
+}
+
+size_t nnop_add_rms_norm_bwd_workspace_size(int64_t emb, int64_t n) { return nnop_rms_norm_bwd_workspace_size(emb, n); }
+
+int nnop_add_rms_norm_bwd(const void* dy, const void* dh, const void* h, const void* w, const float* rstd, void* dx,
+                          float* dw, void* workspace, size_t workspace_bytes, int64_t emb, int64_t n, float offset,
+                          int dtype, void* stream) {
+    if (dh == nullptr)
+        return nnop_rms_norm_bwd(dy, h, w, rstd, dx, dw, workspace, workspace_bytes, emb, n, offset, dtype, stream);
+    int st = check_norm_args(emb, n);
+    if (st) return st;
+    if (!dy || !h || !w || !rstd || !dx || !dw) return fail(NNOP_ERR_ARG, "add_rms_norm_bwd: NULL pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n == 0) {
+        if (cudaMemsetAsync(dw, 0, emb * sizeof(float), s) != cudaSuccess)
+            return fail(NNOP_ERR_CUDA, "add_rms_norm_bwd: memset failed");
+        return NNOP_OK;
+    }
+    if (!workspace || workspace_bytes < nnop_rms_norm_bwd_workspace_size(emb, n))
+        return fail(NNOP_ERR_WORKSPACE, "add_rms_norm_bwd: workspace too small");
+    float* partial = (float*)workspace;
+    int parts = 0;
+    bool fused = false;
+    NNOP_DISPATCH_DTYPE(dtype, T, {
+        fused = ring::rms_bwd_add<T>((const T*)dy, (const T*)dh, (const T*)h, (const T*)w, rstd, (T*)dx, partial,
+                                     (int)emb, n, offset, (int)bwd_max_parts(n), s, &parts, &st);
+    });
+    if (!fused) {
+        st = nnop_rms_norm_bwd(dy, h, w, rstd, dx, dw, workspace, workspace_bytes, emb, n, offset, dtype, stream);
+        if (st) return st;
+        NNOP_DISPATCH_DTYPE(dtype, T, { return launch_add<T>((const T*)dx, (const T*)dh, (T*)dx, emb * n, s); });
+    }
+    if (st) return st;
+    reduce_partials_kernel<float><<<(unsigned)((emb + 255) / 256), 256, 0, s>>>(partial, dw, (int)emb, emb, parts);
+    return check_launch("add_rms_norm_bwd reduce");
 }
 
 }  // extern "C"

@@ -55,7 +55,7 @@ struct Ring {
     uint64_t* full;
     __device__ uint8_t* at(int s, int t) const { return base + ((size_t)s * NT + t) * slot; }
     // thread 0: copy row `row` of the NT tensors into buffer it % S
-    __device__ void issue(int64_t it, int64_t row, const void* const (&src)[NT]) const {
+    __device__ void issue(int64_t it, int64_t row, const void* const* src) const {
         const int s = (int)(it % S);
         mbar_expect_tx(&full[s], NT * row_bytes);
 #pragma unroll
@@ -182,6 +182,16 @@ __device__ __forceinline__ void store_pairs<__half>(__half* dst, const float2* p
     __stcs(reinterpret_cast<uint4*>(dst), make_uint4(u[0], u[1], u[2], u[3]));
 }
 
+// A pair rounded to T and widened back (the values a T tensor stores).
+template <typename T>
+__device__ __forceinline__ float2 round_pair(float2 v);
+template <>
+__device__ __forceinline__ float2 round_pair<float>(float2 v) { return v; }
+template <>
+__device__ __forceinline__ float2 round_pair<__nv_bfloat16>(float2 v) { return __bfloat1622float2(__float22bfloat162_rn(v)); }
+template <>
+__device__ __forceinline__ float2 round_pair<__half>(float2 v) { return __half22float2(__float22half2_rn(v)); }
+
 // The thread's NV vectors of a row-length array in global memory (w, b), as float2 pairs.
 template <typename T, int NV>
 __device__ __forceinline__ void load_pairs(float2 (&out)[NV][8 / sizeof(T)], const T* src, int nvec, float add) {
@@ -255,13 +265,81 @@ rms_fwd_ring_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restr
     if (it < c.rows) ring_drain(r, it, issued);
 }
 
-// ---------------------------------------------------------------- RMSNorm bwd
-// dx = rstd·m − rstd³/N·(Σ m∘x)·x with m = dy∘(w+offset); dw partial += dy∘x·rstd
+// ---------------------------------------------------------------- residual add + RMSNorm fwd
+// h = x + residual, stored in T (the values a separate add would store), and
+// y = (w + offset)·h·rstd(h): one pass over x and residual instead of an add
+// pass and a norm pass that reads h back.
 template <typename T, int NV>
+__global__ void __launch_bounds__(kRingThreads, NV * 16 / sizeof(T) <= 16 ? 2 : 1)
+add_rms_fwd_ring_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
+                        T* __restrict__ h, T* __restrict__ y, float* __restrict__ rstd_out, int emb, int64_t n,
+                        float eps, float offset, float inv_emb, int S) {
+    constexpr int V = 16 / sizeof(T), P = V / 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kMaxStages];
+    __shared__ float red[32];
+    __shared__ int s_abort;
+    if (threadIdx.x == 0) s_abort = 0;
+    const int nvec = emb / V, tid = threadIdx.x;
+    const RingCtl c = ring_ctl(n);
+    const Ring<2> r = ring_init<2>(smem, full, emb, sizeof(T), S);
+    const void* const src[2] = {x, res};
+    int64_t issued = 0;
+    if (tid == 0)
+        for (; issued < c.rows && issued < S; ++issued) r.issue(issued, c.first + issued * c.stride, src);
+    float2 wo[NV][P];
+    load_pairs<T, NV>(wo, w, nvec, offset);
+    int64_t it = 0;
+    for (; it < c.rows; ++it) {
+        const int64_t row = c.first + it * c.stride;
+        if (!ring_wait_all(r, it, &s_abort)) break;
+        const int s = (int)(it % S);
+        Vec<T, V> xv[NV], rv[NV];
+        load_slot<T, NV>(xv, r.at(s, 0), nvec);
+        load_slot<T, NV>(rv, r.at(s, 1), nvec);
+        float2 hv[NV][P];
+        float2 acc = f2(0.f);
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+#pragma unroll
+            for (int j = 0; j < P; ++j) {
+                hv[i][j] = round_pair<T>(add2(pair_f2<T>(xv[i], j), pair_f2<T>(rv[i], j)));
+                if (tid + i * kRingThreads < nvec) acc = fma2(hv[i][j], hv[i][j], acc);
+            }
+        float ss[1] = {acc.x + acc.y};
+        block_sum<1>(ss, red);
+        if (tid == 0 && it + S < c.rows) {
+            fence_proxy_async_smem();
+            r.issue(it + S, c.first + (it + S) * c.stride, src);
+            issued = it + S + 1;
+        }
+        const float rs = 1.0f / sqrtf(ss[0] * inv_emb + eps);
+        if (tid == 0) rstd_out[row] = rs;
+        const float2 rs2 = f2(rs);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int idx = tid + i * kRingThreads;
+            if (idx < nvec) {
+                float2 o[P];
+#pragma unroll
+                for (int j = 0; j < P; ++j) o[j] = mul2(mul2(hv[i][j], rs2), wo[i][j]);
+                store_pairs<T>(h + row * (int64_t)emb + idx * V, hv[i]);
+                store_pairs<T>(y + row * (int64_t)emb + idx * V, o);
+            }
+        }
+    }
+    if (it < c.rows) ring_drain(r, it, issued);
+}
+
+// ---------------------------------------------------------------- RMSNorm bwd
+// dx = rstd·m − rstd³/N·(Σ m∘x)·x with m = dy∘(w+offset); dw partial += dy∘x·rstd.
+// ADD: dx += dh, a third streamed tensor (the residual stream's gradient of
+// the fused residual add + RMSNorm).
+template <typename T, int NV, bool ADD = false>
 __global__ void __launch_bounds__(kRingThreads, NV * 16 / sizeof(T) <= 16 ? 2 : 1)
 rms_bwd_ring_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,
                     const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ partial, int emb,
-                    int64_t n, float offset, float inv_emb, int S) {
+                    int64_t n, float offset, float inv_emb, int S, const T* __restrict__ dh) {
     constexpr int V = 16 / sizeof(T), P = V / 2;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kMaxStages];
@@ -270,8 +348,9 @@ rms_bwd_ring_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* 
     if (threadIdx.x == 0) s_abort = 0;
     const int nvec = emb / V, tid = threadIdx.x;
     const RingCtl c = ring_ctl(n);
-    const Ring<2> r = ring_init<2>(smem, full, emb, sizeof(T), S);
-    const void* const src[2] = {x, dy};
+    constexpr int NT = ADD ? 3 : 2;
+    const Ring<NT> r = ring_init<NT>(smem, full, emb, sizeof(T), S);
+    const void* const src[3] = {x, dy, dh};
     int64_t issued = 0;
     if (tid == 0)
         for (; issued < c.rows && issued < S; ++issued) r.issue(issued, c.first + issued * c.stride, src);
@@ -287,9 +366,10 @@ rms_bwd_ring_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* 
         const float rs = rstd[row];
         if (!ring_wait_all(r, it, &s_abort)) break;
         const int s = (int)(it % S);
-        Vec<T, V> xv[NV], dv[NV];
+        Vec<T, V> xv[NV], dv[NV], hv[ADD ? NV : 1];
         load_slot<T, NV>(xv, r.at(s, 0), nvec);
         load_slot<T, NV>(dv, r.at(s, 1), nvec);
+        if constexpr (ADD) load_slot<T, NV>(hv, r.at(s, NT - 1), nvec);   // before the buffer is refilled
         float2 acc = f2(0.f);
 #pragma unroll
         for (int i = 0; i < NV; ++i)
@@ -311,9 +391,11 @@ rms_bwd_ring_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* 
             if (idx < nvec) {
                 float2 o[P];
 #pragma unroll
+#pragma unroll
                 for (int j = 0; j < P; ++j) {
                     const float2 d2 = pair_f2<T>(dv[i], j), x2 = pair_f2<T>(xv[i], j);
                     o[j] = fma2(crs2, x2, mul2(rs2, mul2(d2, wo[i][j])));
+                    if constexpr (ADD) o[j] = add2(o[j], pair_f2<T>(hv[i], j));
                     dwa[i][j] = fma2(d2, mul2(x2, rs2), dwa[i][j]);
                 }
                 store_pairs<T>(dx + row * (int64_t)emb + idx * V, o);
@@ -596,9 +678,45 @@ bool rms_bwd(const T* dy, const T* x, const T* w, const float* rstd, T* dx, floa
         if (g == 0) return false;
         if (g > max_parts) g = max_parts;
         *parts = g;
-        kern<<<g, kRingThreads, p.smem, s>>>(dy, x, w, rstd, dx, partial, emb, n, offset, 1.0f / (float)emb, p.S);
+        kern<<<g, kRingThreads, p.smem, s>>>(dy, x, w, rstd, dx, partial, emb, n, offset, 1.0f / (float)emb, p.S,
+                                              nullptr);
     });
     *st = check_launch("rms_norm_bwd (ring)");
+    return true;
+}
+
+template <typename T>
+bool add_rms_fwd(const T* x, const T* res, const T* w, T* h, T* y, float* rstd, int emb, int64_t n, float eps,
+                 float offset, cudaStream_t s, int* st) {
+    const RingPlan p = plan_ring<T>(emb, 2, {x, res, w, h, y});
+    if (!p.ok) return false;
+    NNOP_RING_NV_SWITCH(p.nv, NVC, {
+        auto kern = add_rms_fwd_ring_kernel<T, NVC>;
+        const int g = ring_grid(kern, p.smem, n, 8);
+        if (g == 0) return false;
+        kern<<<g, kRingThreads, p.smem, s>>>(x, res, w, h, y, rstd, emb, n, eps, offset, 1.0f / (float)emb, p.S);
+    });
+    *st = check_launch("add_rms_norm_fwd (ring)");
+    return true;
+}
+
+// RMSNorm backward plus dh (the fused residual add's gradient): every dtype
+// through the ring when it applies.
+template <typename T>
+bool rms_bwd_add(const T* dy, const T* dh, const T* x, const T* w, const float* rstd, T* dx, float* partial, int emb,
+                 int64_t n, float offset, int max_parts, cudaStream_t s, int* parts, int* st) {
+    const RingPlan p = plan_ring<T>(emb, 3, {dy, dh, x, w, dx}, 32);
+    if (!p.ok) return false;
+    NNOP_RING_NV_SWITCH(p.nv, NVC, {
+        auto kern = rms_bwd_ring_kernel<T, NVC, true>;
+        int g = ring_grid(kern, p.smem, n, 8);
+        if (g == 0) return false;
+        if (g > max_parts) g = max_parts;
+        *parts = g;
+        kern<<<g, kRingThreads, p.smem, s>>>(dy, x, w, rstd, dx, partial, emb, n, offset, 1.0f / (float)emb, p.S,
+                                              dh);
+    });
+    *st = check_launch("add_rms_norm_bwd (ring)");
     return true;
 }
 
@@ -642,7 +760,11 @@ bool ln_bwd(const T* dy, const T* x, const T* w, const float* mean, const float*
     template bool ln_fwd<T>(const T*, const T*, const T*, T*, float*, float*, int, int64_t, float, cudaStream_t, \
                             int*);                                                                               \
     template bool ln_bwd<T>(const T*, const T*, const T*, const float*, const float*, T*, float*, int, int64_t,  \
-                            int, cudaStream_t, int*, int*);
+                            int, cudaStream_t, int*, int*);                                                      \
+    template bool add_rms_fwd<T>(const T*, const T*, const T*, T*, T*, float*, int, int64_t, float, float,        \
+                                 cudaStream_t, int*);                                                            \
+    template bool rms_bwd_add<T>(const T*, const T*, const T*, const T*, const float*, T*, float*, int, int64_t,  \
+                                 float, int, cudaStream_t, int*, int*);
 NNOP_RING_INST(float)
 NNOP_RING_INST(__half)
 NNOP_RING_INST(__nv_bfloat16)

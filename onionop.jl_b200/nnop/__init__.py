@@ -31,8 +31,10 @@ from ._lib import (BF16, F16, F32, NNopError, NNopShapeError, check, lib)
 __all__ = [
     "flash_attention", "_flash_attention", "grad_flash_attention",
     "flash_attention_pair_per_head", "_flash_attention_pair_per_head", "grad_flash_attention_pair_per_head",
+    "flash_attention_rope", "_flash_attention_rope", "grad_flash_attention_rope",
     "online_softmax", "grad_online_softmax",
     "rms_norm", "_rms_norm", "grad_rms_norm",
+    "add_rms_norm", "_add_rms_norm", "grad_add_rms_norm",
     "layer_norm", "_layer_norm", "grad_layer_norm",
     "llama_rope", "grad_llama_rope", "LlamaRotaryEmbedding",
     "within_gradient", "NNopError", "NNopShapeError", "lib",
@@ -273,6 +275,86 @@ def flash_attention_pair_per_head(q, k, v, pair, *, causal: bool, kpad_mask=None
     return _flash_attention_pair_per_head(q, k, v, pair, causal=causal, kpad_mask=kpad_mask)[0]
 
 
+# -------------------------------------------------------------------------
+# Llama RoPE fused with attention: flash_attention(llama_rope(q, k)...)
+# -------------------------------------------------------------------------
+
+def _rope_tables(cos, sin, B, L, E):
+    cos = cos.contiguous().to(torch.float32)
+    sin = sin.contiguous().to(torch.float32)
+    if cos.dim() == 2:
+        cos, sin = cos[None], sin[None]
+    if cos.shape != sin.shape or cos.shape[1] != L or cos.shape[2] != E or cos.shape[0] not in (1, B):
+        raise NNopShapeError(-1, "cos/sin must have shape (B or 1, L, E)")
+    return cos, sin
+
+
+def _flash_attention_rope(q, k, v, *, cos, sin, causal: bool, kpad_mask=None):
+    """``llama_rope`` then ``_flash_attention`` in one call: returns
+    ``(o, lse, q_rot, k_rot)``; the rotated q and k are the backward's inputs.
+    bf16/f16, E = 64 or 128, q and k of one length L."""
+    dev = _dev(q, k, v, cos, sin, kpad_mask)
+    B, QH, QL, E, KH, KL = _fa_dims(q, k, v, None, kpad_mask)
+    if QL != KL:
+        raise NNopShapeError(-1, "q and k must share the sequence length")
+    cos, sin = _rope_tables(cos, sin, B, QL, E)
+    q, k, v = _contig(q), _contig(k), _contig(v)
+    m = _mask_u8(kpad_mask)
+    qr, kr, o = torch.empty_like(q), torch.empty_like(k), torch.empty_like(q)
+    lse = torch.empty((B, QH, QL), dtype=torch.float32, device=dev)
+    check(lib.nnop_flash_attention_rope_fwd(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(cos), _ptr(sin), _ptr(m), _ptr(qr), _ptr(kr), _ptr(o), _ptr(lse),
+        E, QL, QH, KH, B, cos.shape[0], int(bool(causal)), _dtype_id(q), _stream(dev)))
+    return o, lse, qr, kr
+
+
+def grad_flash_attention_rope(do, o, lse, q_rot, k_rot, v, *, cos, sin, causal: bool, kpad_mask=None):
+    """Backward of ``_flash_attention_rope``: ``(dq, dk, dv)`` with dq, dk the
+    gradients of the UN-rotated q and k (``∇llama_rope`` folded into the
+    attention backward's outputs)."""
+    dev = _dev(do, o, lse, q_rot, k_rot, v, cos, sin, kpad_mask)
+    B, QH, L, E, KH, _ = _fa_dims(q_rot, k_rot, v, None, kpad_mask)
+    cos, sin = _rope_tables(cos, sin, B, L, E)
+    do, o, q_rot, k_rot, v = map(_contig, (do, o, q_rot, k_rot, v))
+    if do.dtype != q_rot.dtype:
+        do = do.to(q_rot.dtype)
+    m = _mask_u8(kpad_mask)
+    dq, dk, dv = torch.empty_like(q_rot), torch.empty_like(k_rot), torch.empty_like(v)
+    dt = _dtype_id(q_rot)
+    ws_bytes = lib.nnop_flash_attention_rope_bwd_workspace_size(E, L, QH, KH, B, dt)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    check(lib.nnop_flash_attention_rope_bwd(
+        _ptr(do), _ptr(o), _ptr(lse.contiguous()), _ptr(q_rot), _ptr(k_rot), _ptr(v), _ptr(cos), _ptr(sin), _ptr(m),
+        _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws_bytes, E, L, QH, KH, B, cos.shape[0], int(bool(causal)), dt,
+        _stream(dev)))
+    return dq, dk, dv
+
+
+class _FlashAttentionRopeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cos, sin, kpad_mask, causal):
+        o, lse, qr, kr = _flash_attention_rope(q, k, v, cos=cos, sin=sin, causal=causal, kpad_mask=kpad_mask)
+        ctx.save_for_backward(o, lse, qr, kr, v, cos, sin, kpad_mask)
+        ctx.causal = causal
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        o, lse, qr, kr, v, cos, sin, kpad_mask = ctx.saved_tensors
+        dq, dk, dv = grad_flash_attention_rope(do, o, lse, qr, kr, v, cos=cos, sin=sin, causal=ctx.causal,
+                                               kpad_mask=kpad_mask)
+        return dq, dk, dv, None, None, None, None
+
+
+def flash_attention_rope(q, k, v, *, cos, sin, causal: bool, kpad_mask=None):
+    """``flash_attention(llama_rope(q, k; cos, sin)..., v)`` with the RoPE
+    backward folded into the attention backward; differentiable w.r.t. the
+    un-rotated q, k and v."""
+    if any(within_gradient(t) for t in (q, k, v)):
+        return _FlashAttentionRopeFn.apply(q, k, v, cos, sin, kpad_mask, bool(causal))
+    return _flash_attention_rope(q, k, v, cos=cos, sin=sin, causal=causal, kpad_mask=kpad_mask)[0]
+
+
 # =========================================================================
 # online softmax   (src/softmax.jl)
 # =========================================================================
@@ -384,6 +466,74 @@ def rms_norm(x, w, *, eps: float = 1e-6, offset: float = 0.0):
     if within_gradient(x) or within_gradient(w):
         return _RmsNormFn.apply(x, w, float(eps), float(offset))
     return _rms_norm(x, w, eps=eps, offset=offset)[0]
+
+
+# -------------------------------------------------------------------------
+# residual add fused into RMSNorm (the composition a transformer block makes
+# around rms_norm; no counterpart in the reference's API)
+# -------------------------------------------------------------------------
+
+def _add_rms_norm(x, residual, w, *, eps: float = 1e-6, offset: float = 0.0):
+    """``h = x + residual`` (rounded to the dtype) and ``rms_norm(h, w)`` in one
+    pass: returns ``(y, h, rstd)``."""
+    dev = _dev(x, residual, w)
+    if residual.shape != x.shape or residual.dtype != x.dtype:
+        raise NNopShapeError(-1, "residual must have the shape and dtype of x")
+    x, residual = x.contiguous(), residual.contiguous()
+    w = w.contiguous().to(x.dtype)
+    emb, n = _norm_dims(x, w)
+    h, y = torch.empty_like(x), torch.empty_like(x)
+    rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=dev)
+    check(lib.nnop_add_rms_norm_fwd(_ptr(x), _ptr(residual), _ptr(w), _ptr(h), _ptr(y), _ptr(rstd), emb, n,
+                                    float(eps), float(offset), _dtype_id(x), _stream(dev)))
+    return y, h, rstd
+
+
+def grad_add_rms_norm(dy, dh, h, w, rstd, *, offset: float = 0.0):
+    """Backward of ``_add_rms_norm``: ``dx = ∇rms_norm(dy, h) + dh`` (dh, the
+    gradient reaching h from the residual stream, may be None) -- the gradient
+    of both x and residual -- and ``dw`` (float32)."""
+    dev = _dev(dy, h, w, rstd)
+    h = h.contiguous()
+    w = w.contiguous().to(h.dtype)
+    dy = dy.contiguous().to(h.dtype)
+    if dh is not None:
+        dh = dh.contiguous().to(h.dtype)
+    emb, n = _norm_dims(h, w)
+    dx = torch.empty_like(h)
+    dw = torch.empty(emb, dtype=torch.float32, device=dev)
+    ws_bytes = lib.nnop_add_rms_norm_bwd_workspace_size(emb, n)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    check(lib.nnop_add_rms_norm_bwd(_ptr(dy), _ptr(dh), _ptr(h), _ptr(w), _ptr(rstd.contiguous()), _ptr(dx),
+                                    _ptr(dw), _ptr(ws), ws_bytes, emb, n, float(offset), _dtype_id(h), _stream(dev)))
+    return dx, dw
+
+
+class _AddRmsNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, residual, w, eps, offset):
+        y, h, rstd = _add_rms_norm(x, residual, w, eps=eps, offset=offset)
+        ctx.save_for_backward(h, w, rstd)
+        ctx.offset = offset
+        return y, h
+
+    @staticmethod
+    def backward(ctx, dy, dh):
+        h, w, rstd = ctx.saved_tensors
+        if dy is None:
+            dy = torch.zeros_like(h)
+        dx, dw = grad_add_rms_norm(dy, dh, h, w, rstd, offset=ctx.offset)
+        return dx, dx, dw.to(w.dtype).reshape(w.shape), None, None
+
+
+def add_rms_norm(x, residual, w, *, eps: float = 1e-6, offset: float = 0.0):
+    """Residual add and ``rms_norm`` fused: returns ``(y, h)`` with
+    ``h = x + residual`` (the new residual stream) and ``y = rms_norm(h, w)``;
+    differentiable w.r.t. x, residual and w."""
+    if any(within_gradient(t) for t in (x, residual, w)):
+        return _AddRmsNormFn.apply(x, residual, w, float(eps), float(offset))
+    y, h, _ = _add_rms_norm(x, residual, w, eps=eps, offset=offset)
+    return y, h
 
 
 # =========================================================================

@@ -47,12 +47,20 @@ SIGNATURES = {
     "nnop_flash_attention_bwd_pair_per_head": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                                       _vp, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int,
                                                       _vp]),
+    "nnop_flash_attention_rope_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                             _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
+    "nnop_flash_attention_rope_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
+    "nnop_flash_attention_rope_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                                             _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "nnop_online_softmax_fwd": (_int, [_vp, _vp, _i64, _i64, _int, _vp]),
     "nnop_online_softmax_bwd": (_int, [_vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "nnop_rms_norm_fwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f, _f, _int, _vp]),
     "nnop_rms_norm_bwd_workspace_size": (_sz, [_i64, _i64]),
     "nnop_rms_norm_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _f, _int, _vp]),
     "nnop_rms_norm_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _vp]),
+    "nnop_add_rms_norm_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _f, _int, _vp]),
+    "nnop_add_rms_norm_bwd_workspace_size": (_sz, [_i64, _i64]),
+    "nnop_add_rms_norm_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _f, _int, _vp]),
     "nnop_layer_norm_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _vp]),
     "nnop_layer_norm_bwd_workspace_size": (_sz, [_i64, _i64]),
     "nnop_layer_norm_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),

@@ -68,6 +68,7 @@ __all__ = [
     "attention_scale", "round_to", "attention_fwd", "attention_bwd",
     "softmax_fwd", "softmax_bwd", "rms_norm_fwd", "rms_norm_bwd",
     "layer_norm_fwd", "layer_norm_bwd", "rope_fwd", "rope_bwd",
+    "add_rms_norm_fwd", "add_rms_norm_bwd",
     "llama_rotary_embedding", "rel_err", "max_abs_err",
 ]
 
@@ -269,6 +270,27 @@ def rms_norm_bwd(dy, x, w, *, eps=1e-6, offset=0.0):
     dd = np.sum(m * x, axis=-1)
     dx = rstd[:, None] * m - (rstd ** 3 * dd / N)[:, None] * x
     dw = np.sum(dy * x * rstd[:, None], axis=0)
+    return dx, dw
+
+
+def add_rms_norm_fwd(x, residual, w, *, eps=1e-6, offset=0.0, dtype="f32"):
+    """Residual add followed by ``rms_norm`` -- the composition a transformer
+    block performs around the reference's ``rms_norm`` (src/rms_norm.jl:171):
+    h = x + residual, rounded to the tensors' dtype as a separate add would
+    store it, then ``rms_norm_fwd(h, w)``.  Returns ``(y, h, rstd)``."""
+    h = round_to(np.asarray(x, np.float64) + np.asarray(residual, np.float64), dtype)
+    y, rstd = rms_norm_fwd(h, w, eps=eps, offset=offset)
+    return y, h, rstd
+
+
+def add_rms_norm_bwd(dy, dh, h, w, *, eps=1e-6, offset=0.0):
+    """Gradients of ``add_rms_norm_fwd``: the gradient reaching h is
+    ``rms_norm_bwd(dy, h, w)`` plus ``dh`` (the gradient arriving at h from
+    its other use, the residual stream; None = 0); it is the gradient of both
+    x and residual.  Returns ``(dx, dw)``."""
+    dx, dw = rms_norm_bwd(dy, h, w, eps=eps, offset=offset)
+    if dh is not None:
+        dx = dx + np.asarray(dh, np.float64)
     return dx, dw
 
 
