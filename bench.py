@@ -365,6 +365,13 @@ def measure_memory(dev, K: int, W: int) -> dict:
         y, mu, rs = nnop._layer_norm(x, w, b)
         add(f"layer_norm_fwd_{tag}", 2 * n * emb * es, timed(lambda: nnop._layer_norm(x, w, b)))
         add(f"layer_norm_bwd_{tag}", 3 * n * emb * es, timed(lambda: nnop.grad_layer_norm(dy, mu, rs, x, w)))
+        if tag == "bf16":
+            # residual add fused into RMSNorm: read x, residual, write h, y;
+            # backward read dy, h, dh, write dx (x and dy stand in for residual and dh)
+            y, h, rh = nnop._add_rms_norm(x, dy, w)
+            add("add_rms_norm_fwd_bf16", 4 * n * emb * es, timed(lambda: nnop._add_rms_norm(x, dy, w)))
+            add("add_rms_norm_bwd_bf16", 4 * n * emb * es, timed(lambda: nnop.grad_add_rms_norm(dy, x, h, w, rh)))
+            del h
         del x, dy, y
         torch.cuda.empty_cache()
     x = 4 * torch.randn(16384, 8192, device=dev, generator=g)
@@ -443,6 +450,12 @@ def measure_config3(dev, K: int, W: int, B: int = 4) -> dict:
     o3, lse3 = nnop._flash_attention(qr, kr, v, causal=True)
     ms_bwd = timed(lambda: nnop.grad_flash_attention(do, o3, lse3, qr, kr, v, causal=True))
     ms = timed(step3)
+
+    def step3_fused():
+        # RoPE fused with attention: the inverse rotation folded into the backward
+        o, lse, qr, kr = nnop._flash_attention_rope(q, k, v, cos=cos, sin=sin, causal=True)
+        nnop.grad_flash_attention_rope(do, o, lse, qr, kr, v, cos=cos, sin=sin, causal=True)
+    ms_fused = timed(step3_fused)
     f = 14.0 * B * QH * L * L * E * 0.5
     rope_bytes = 2 * (2 * (q.numel() + k.numel()) * 2 + 2 * cos.numel() * 4)
     out = {
@@ -452,7 +465,9 @@ def measure_config3(dev, K: int, W: int, B: int = 4) -> dict:
         "attention_frac": f / (ms_attn / 1e3) / 1e12 / tc,
         "fwd_ms": ms_fwd, "fwd_TFLOP/s": f / 3.5 / (ms_fwd / 1e3) / 1e12,
         "bwd_ms": ms_bwd, "bwd_TFLOP/s": f / 3.5 * 2.5 / (ms_bwd / 1e3) / 1e12,
-        "rope_fwd_bwd_bytes": rope_bytes, "B": B}
+        "rope_fwd_bwd_bytes": rope_bytes, "B": B,
+        "rope_fused_ms": ms_fused, "rope_fused_TFLOP/s": f / (ms_fused / 1e3) / 1e12,
+        "rope_fused_frac": f / (ms_fused / 1e3) / 1e12 / tc}
     del o3, lse3, q, k, v, do, qr, kr, cos, sin, pos
     torch.cuda.empty_cache()
     return out
