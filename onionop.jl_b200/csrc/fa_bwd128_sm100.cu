@@ -357,6 +357,12 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
                     tmem_ld32(src + 64 + c * 32, rb);
                     tmem_ld_wait();
                     if (j < KL) {
+                        float4 cw[8], sw[8];   // cos/sin of indices 32c .. 32c+31 at position j
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            cw[v] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + tr + 32 * c) + v);
+                            sw[v] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + tr + 32 * c) + v);
+                        }
                         uint32_t pa[16], pb[16];
 #pragma unroll
                         for (int u = 0; u < 32; u += 2) {
@@ -365,8 +371,8 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
                             for (int v = 0; v < 2; ++v) {
                                 const float a = steps > 0 ? __uint_as_float(ra[u + v]) * mul : 0.f;
                                 const float bb = steps > 0 ? __uint_as_float(rb[u + v]) * mul : 0.f;
-                                const float cs = __ldg(p.rope_cos + tr + 32 * c + u + v);
-                                const float sn = __ldg(p.rope_sin + tr + 32 * c + u + v);
+                                const float cs = reinterpret_cast<const float*>(cw)[u + v];
+                                const float sn = reinterpret_cast<const float*>(sw)[u + v];
                                 oa[v] = a * cs + bb * sn;
                                 ob[v] = bb * cs - a * sn;
                             }

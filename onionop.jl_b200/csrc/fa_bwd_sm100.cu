@@ -402,6 +402,12 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     tmem_ld16(src + 32 + c * 16, rb);
                     tmem_ld_wait();
                     if (j < KL) {
+                        float4 cw[4], sw[4];   // cos/sin of indices 16c .. 16c+15 at position j
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            cw[v] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + tr + 16 * c) + v);
+                            sw[v] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + tr + 16 * c) + v);
+                        }
                         uint32_t pa[8], pb[8];
 #pragma unroll
                         for (int u = 0; u < 16; u += 2) {
@@ -410,8 +416,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                             for (int v = 0; v < 2; ++v) {
                                 const float a = tiles > 0 ? __uint_as_float(ra[u + v]) * mul : 0.f;
                                 const float bb = tiles > 0 ? __uint_as_float(rb[u + v]) * mul : 0.f;
-                                const float cs = __ldg(p.rope_cos + tr + 16 * c + u + v);
-                                const float sn = __ldg(p.rope_sin + tr + 16 * c + u + v);
+                                const float cs = reinterpret_cast<const float*>(cw)[u + v];
+                                const float sn = reinterpret_cast<const float*>(sw)[u + v];
                                 oa[v] = a * cs + bb * sn;
                                 ob[v] = bb * cs - a * sn;
                             }

@@ -101,15 +101,18 @@ __global__ void convert_rope_kernel(const float* __restrict__ src, T* __restrict
     const float4 sn = *reinterpret_cast<const float4*>(sin_t + tr);
     const float4 a = __ldcs(reinterpret_cast<const float4*>(src + row * E + e));
     const float4 bb = __ldcs(reinterpret_cast<const float4*>(src + row * E + e + half));
-    T* d = dst + row * E + e;
-    d[0] = from_f<T>(a.x * c.x + bb.x * sn.x);
-    d[1] = from_f<T>(a.y * c.y + bb.y * sn.y);
-    d[2] = from_f<T>(a.z * c.z + bb.z * sn.z);
-    d[3] = from_f<T>(a.w * c.w + bb.w * sn.w);
-    d[half + 0] = from_f<T>(bb.x * c.x - a.x * sn.x);
-    d[half + 1] = from_f<T>(bb.y * c.y - a.y * sn.y);
-    d[half + 2] = from_f<T>(bb.z * c.z - a.z * sn.z);
-    d[half + 3] = from_f<T>(bb.w * c.w - a.w * sn.w);
+    // 8-byte stores of the 4 results of each half
+    Vec<T, 4> lo, hi;
+    lo.v[0] = from_f<T>(a.x * c.x + bb.x * sn.x);
+    lo.v[1] = from_f<T>(a.y * c.y + bb.y * sn.y);
+    lo.v[2] = from_f<T>(a.z * c.z + bb.z * sn.z);
+    lo.v[3] = from_f<T>(a.w * c.w + bb.w * sn.w);
+    hi.v[0] = from_f<T>(bb.x * c.x - a.x * sn.x);
+    hi.v[1] = from_f<T>(bb.y * c.y - a.y * sn.y);
+    hi.v[2] = from_f<T>(bb.z * c.z - a.z * sn.z);
+    hi.v[3] = from_f<T>(bb.w * c.w - a.w * sn.w);
+    *reinterpret_cast<Vec<T, 4>*>(dst + row * E + e) = lo;
+    *reinterpret_cast<Vec<T, 4>*>(dst + row * E + e + half) = hi;
 }
 
 }  // namespace
