@@ -23,6 +23,7 @@ int sm100_bwd_tile();
 int sm100_fwd_timeouts();
 int sm100_bwd_timeouts();
 int sm100_bwd128_timeouts();
+int sm100_fwd2_timeouts();
 }  // namespace fa
 
 namespace fa_host {
@@ -237,7 +238,7 @@ int nnop_kernel_timing_read(int which, double* total_ms, int* count) {
 }
 
 int nnop_device_wait_timeouts(void) {
-    const int f = fa::sm100_fwd_timeouts();
+    const int f = fa::sm100_fwd_timeouts() | fa::sm100_fwd2_timeouts();
     const int b = fa::sm100_bwd_timeouts() | fa::sm100_bwd128_timeouts();
     return (f & 0xffff) | ((b & 0x7fff) << 16);
 }

@@ -585,3 +585,122 @@ def backward128(T: int, seed: int, plant: str | None = None, slow_tma: bool = Fa
     for wi in range(4):
         roles[f"dq{wi}"] = dq_warp(wi)
     sim.run(roles)
+
+
+# ------------------------------------------------------------------ forward, two tiles (no pair)
+def forward2(nkt0: int, nkt1: int, seed: int, stages: int = 2, rescale_p: float = 0.5,
+             plant: str | None = None, slow_tma: bool = False):
+    """fa_fwd2_sm100_kernel: two query tiles per CTA, one S buffer and one O
+    accumulator per tile, one K/V ring both tiles read.  Per key tile j the MMA
+    warp waits V_j (and K_{j+1}), then per tile t: PFull_t(j) -> PV_t(j),
+    OStep_t, and S_t(j+1) behind it (same TMEM columns as P_t(j)) or OFinal_t;
+    KVEmpty_j once both tiles' MMAs of step j are issued.  With a causal mask
+    the second tile has one key tile more (nkt1 = nkt0 + 1)."""
+    sim = _Sim(seed, slow_tma)
+    S = stages
+    nkt = [nkt0, nkt1]
+    n_kt = max(nkt)
+    sim.bar("QFull")
+    sim.bar("MmaDone")
+    for s in range(S):
+        for n in ("KFull", "VFull", "KVEmpty"):
+            sim.bar(f"{n}{s}")
+    for t in range(2):
+        for n in ("SFull", "PFull", "OStep", "OFinal"):
+            sim.bar(f"{n}{t}")
+    o = {0: 0, 1: 0}
+
+    def producer():
+        yield ("do", lambda: None)
+        if n_kt == 0:
+            return
+        sim.asyncs.append((lambda: sim.mem.__setitem__("Q", "q"), "QFull"))
+        for j in range(n_kt):
+            s = j % S
+            if j >= S:
+                yield _wait(plant, f"KVEmpty{s}", j // S - 1)
+
+            def land_k(j=j, s=s):
+                if j >= S and any(("S", t, j - S + 1) not in sim.executed for t in range(2) if j - S + 1 < nkt[t]):
+                    raise ProtocolBug(f"K stage {s} reloaded before S(j={j - S + 1}) read it")
+                sim.mem[f"K{s}"] = j
+
+            def land_v(j=j, s=s):
+                if j >= S and any(("PV", t, j - S) not in sim.executed for t in range(2) if j - S < nkt[t]):
+                    raise ProtocolBug(f"V stage {s} reloaded before PV({j - S}) read it")
+                sim.mem[f"V{s}"] = j
+            sim.asyncs.append((land_k, f"KFull{s}"))
+            sim.asyncs.append((land_v, f"VFull{s}"))
+
+    def mma():
+        if n_kt == 0:
+            yield ("do", lambda: None)
+            return
+        yield ("wait", "QFull", 0)
+
+        def issue_s(t, j):
+            def run(t=t, j=j):
+                sim.expect("Q", "q")
+                sim.expect(f"K{j % S}", j)
+                if j > 0 and ("PV", t, j - 1) not in sim.executed:
+                    raise ProtocolBug(f"S_{t}({j}) overwrites P_{t}({j - 1}) before PV read it")
+                sim.mem[f"S{t}"] = ("S", j)
+            sim.mma(("S", t, j), run)
+            sim.commit(f"SFull{t}")
+
+        yield _wait(plant, "KFull0", 0)
+        for t in range(2):
+            if nkt[t] > 0:
+                issue_s(t, 0)
+        for j in range(n_kt):
+            s = j % S
+            yield _wait(plant, f"VFull{s}", j // S)
+            if j + 1 < n_kt:
+                yield _wait(plant, f"KFull{(j + 1) % S}", (j + 1) // S)
+            for t in range(2):
+                if j >= nkt[t]:
+                    continue
+                yield _wait(plant, f"PFull{t}", j)
+
+                def pv(t=t, j=j, s=s):
+                    sim.expect(f"S{t}", ("P", j))
+                    sim.expect(f"V{s}", j)
+                    if o[t] != j:
+                        raise ProtocolBug(f"O_{t} holds {o[t]} products at PV({j})")
+                    o[t] += 1
+                sim.mma(("PV", t, j), pv)
+                sim.commit(f"OStep{t}")
+                if j == nkt[t] - 1:
+                    sim.commit(f"OFinal{t}")
+                else:
+                    issue_s(t, j + 1)
+            sim.commit(f"KVEmpty{s}")
+        sim.commit("MmaDone")
+        yield ("wait", "MmaDone", 0)
+
+    def softmax(t):
+        yield ("do", lambda: None)
+        for j in range(nkt[t]):
+            yield _wait(plant, f"SFull{t}", j)
+
+            def sm(t=t, j=j):
+                sim.expect(f"S{t}", ("S", j))
+                sim.mem[f"S{t}"] = ("P", j)
+            yield ("do", sm)
+            if j > 0 and sim.rng.random() < rescale_p:
+                yield _wait(plant, f"OStep{t}", j - 1)
+
+                def resc(t=t, j=j):
+                    if o[t] != j:
+                        raise ProtocolBug(f"O_{t} rescaled with {o[t]} products at key tile {j}")
+                yield ("do", resc)
+            yield ("arrive", f"PFull{t}")
+        if nkt[t]:
+            yield _wait(plant, f"OFinal{t}", 0)
+
+            def fin(t=t):
+                if o[t] != nkt[t]:
+                    raise ProtocolBug(f"O_{t} read with {o[t]} of {nkt[t]} products")
+            yield ("do", fin)
+
+    sim.run({"producer": producer(), "mma": mma(), "sm0": softmax(0), "sm1": softmax(1)})

@@ -64,3 +64,26 @@ def test_backward128_protocol(slow_tma):
                                    "TileEmpty1"])
 def test_backward128_planted_mistake_is_caught(plant):
     assert _caught(kp.backward128, plant, T=7) or _caught(kp.backward128, plant, T=7, slow_tma=True)
+
+
+@pytest.mark.parametrize("stages", [2, 3])
+@pytest.mark.parametrize("slow_tma", [False, True])
+def test_forward2_protocol(stages, slow_tma):
+    for nkt0, nkt1 in [(0, 0), (1, 0), (1, 1), (1, 2), (3, 3), (4, 5), (6, 6), (2, 3)]:
+        for seed in range(30):
+            kp.forward2(nkt0, nkt1, seed, stages=stages, slow_tma=slow_tma)
+
+
+@pytest.mark.parametrize("plant", ["KVEmpty0", "KVEmpty1", "KFull1", "VFull0", "PFull0", "PFull1", "SFull1",
+                                   "OFinal1"])
+def test_forward2_planted_mistake_is_caught(plant):
+    assert (_caught(kp.forward2, plant, nkt0=4, nkt1=5) or
+            _caught(kp.forward2, plant, nkt0=4, nkt1=5, slow_tma=True))
+
+
+def test_forward2_rescale_wait_is_implied():
+    """In the two-tile forward S_t(j) is issued behind PV_t(j-1) in the same
+    thread's UMMA order, so SFull_t(j) already implies that O_t holds every
+    earlier product: the softmax's OStep wait before a rescale never waits
+    (the model finds no hazard without it).  The kernel keeps it as a guard."""
+    assert not _caught(kp.forward2, "OStep0", nkt0=4, nkt1=5)
