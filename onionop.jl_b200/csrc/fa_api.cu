@@ -41,8 +41,9 @@ namespace {
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // NNOP_B200_FA=mma selects the mma.sync kernels for every shape (used by the
-// tests to check both kernel families); the default picks the tcgen05 kernels
-// where they apply.
+// tests to check both kernel families; NNOP_B200_FA=one_tile selects the
+// one-tile tcgen05 forward, fa_fwd_sm100.cu); the default picks the tcgen05
+// kernels where they apply.
 bool force_mma() {
     const char* e = getenv("NNOP_B200_FA");
     return e != nullptr && e[0] == 'm';

@@ -1,5 +1,5 @@
-// Flash-attention forward without a pair bias on the sm_100a tensor cores,
-// two query tiles per CTA in ping-pong (bf16/f16, E in {64, 128}).
+// Flash-attention forward on the sm_100a tensor cores, two query tiles per
+// CTA in ping-pong (bf16/f16; E in {64, 128}, E = 64 with a pair bias).
 //
 // Reference: `_flash_attention_fwd!` (src/attention.jl:8-143).
 //
@@ -27,6 +27,12 @@
 // TMEM: tile t: S_t [t·W, t·W+128), O_t [t·W+128, t·W+128+E), W = 128 + E.
 // S_t is single-buffered: S_t(j+1) is issued behind PV_t(j), which reads P_t(j)
 // from the same columns (one thread's UMMAs run in order).
+// With a pair bias (E = 64) the producer also loads the pair tile of every
+// (tile, key tile) -- from the per-head tiles pair_tiles() writes or, through
+// the per-head entry points, from the caller's [B][H][KL][QL] buffer -- into
+// a 3-slot ring shared by both tiles in the order the scores are issued
+// (key tile major, tile minor), and the MMA warp adds it to S_t as
+// c·I·pairᵀ (c = 1/scale, exact) with the shifted identity of fa_sm100.cuh.
 // With a causal mask the second tile sees one more key tile than the first.
 // Every mbarrier wait is bounded; waits guarding warp-wide tcgen05.ld/st are
 // warp-uniform.
@@ -61,31 +67,41 @@ enum Bar {
     kOStep = 14,     // +tile: PV_t(j) retired
     kOFinal = 16,    // +tile: every PV_t retired
     kMmaDone = 18,
-    kNumBars = 19
+    kPairFull = 19,  // +slot (TMA -> MMA)
+    kPairEmpty = 22, // +slot (its UMMAs retired -> producer)
+    kNumBars = 25
 };
 
-template <int E>
+constexpr int kPairSlots = 3;
+
+template <int E, bool PAIR>
 struct Layout2 {
-    static constexpr int kStages = E == 64 ? 3 : 2;
+    static constexpr int kStages = (E == 64 && !PAIR) ? 3 : 2;
     static constexpr int kQBytes = kBM * E * 2;
     static constexpr int kKVBytes = kBN * E * 2;
+    static constexpr int kPairBytes = PAIR ? kBN * kBM * 2 : 0;
     static constexpr int kQ = 0;                               // 2 tiles
     static constexpr int kK = kQ + 2 * kQBytes;
     static constexpr int kV = kK + kStages * kKVBytes;
-    static constexpr int kBits = kV + kStages * kKVBytes;
+    static constexpr int kPair = kV + kStages * kKVBytes;
+    static constexpr int kEye = kPair + kPairSlots * kPairBytes;   // 1024-aligned
+    static constexpr int kBits = kEye + (PAIR ? kEyeBytes : 0);
     static constexpr int kBar = kBits + kMaxKeyWords * 4;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kTotal = kTmemSlot + 16;
     static constexpr int kAlloc = kTotal + 1024;               // slack for 1024-byte alignment
 };
-static_assert(Layout2<128>::kAlloc <= 227 * 1024, "shared memory");
-static_assert(Layout2<64>::kAlloc <= 227 * 1024, "shared memory");
+static_assert(Layout2<128, false>::kAlloc <= 227 * 1024, "shared memory");
+static_assert(Layout2<64, false>::kAlloc <= 227 * 1024, "shared memory");
+static_assert(Layout2<64, true>::kAlloc <= 227 * 1024, "shared memory");
 
-template <typename T, int E, bool CAUSAL, bool MASK>
+template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const Params p) {
-    using L = Layout2<E>;
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_pair,
+                     const Params p) {
+    static_assert(!PAIR || E == 64, "pair tiles fit shared memory only for E = 64");
+    using L = Layout2<E, PAIR>;
     constexpr int S = L::kStages;
     constexpr int W = kBN + E;   // TMEM columns per tile
     constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -129,6 +145,10 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             bits[w] = n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
         }
     }
+    if (PAIR) {
+        build_eye<T>(smem + L::kEye, 1.f / p.scale, threadIdx.x, kThreads);
+        fence_proxy_async_smem();   // identity writes -> UMMA reads
+    }
     if (threadIdx.x == 0) {
         s_abort = 0;
         mbar_init(&bars[kQFull], 1);
@@ -142,6 +162,10 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             mbar_init(&bars[kPFull + t], 128);
             mbar_init(&bars[kOStep + t], 1);
             mbar_init(&bars[kOFinal + t], 1);
+        }
+        for (int i = 0; i < kPairSlots; ++i) {
+            mbar_init(&bars[kPairFull + i], 1);
+            mbar_init(&bars[kPairEmpty + i], 1);
         }
         mbar_init(&bars[kMmaDone], 1);
         fence_mbar_init();
@@ -176,6 +200,7 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             tma_prefetch(&tm_q);
             tma_prefetch(&tm_k);
             tma_prefetch(&tm_v);
+            if (PAIR) tma_prefetch(&tm_pair);
             const int bh_q = b * p.QH + h, bh_k = b * p.KH + kvh;
             const int nq = nkt1 > 0 ? 2 : 1;
             mbar_expect_tx(&bars[kQFull], nq * L::kQBytes);
@@ -184,8 +209,32 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 for (int e2 = 0; e2 < E / 64; ++e2)
                     tma_load_3d(smem + L::kQ + t * L::kQBytes + e2 * kBM * 128, &tm_q, &bars[kQFull], e2 * 64,
                                 (2 * pr + t) * kBM, bh_q);
+            // pair tiles of key tile j (both query tiles), the u-th into slot
+            // u % 3 once the scores that read tile u - 3 have retired
+            int pair_issued = 0;
+            auto load_pairs = [&](int j) -> bool {
+                for (int t = 0; t < 2; ++t) {
+                    if (j >= (t ? nkt1 : nkt0)) continue;
+                    const int u = pair_issued, slot = u % kPairSlots;
+                    if (u >= kPairSlots && !wait(&bars[kPairEmpty + slot], ((u / kPairSlots) - 1) & 1, ab, 13))
+                        return false;
+                    mbar_expect_tx(&bars[kPairFull + slot], L::kPairBytes);
+                    const int qt = 2 * pr + t;
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        uint8_t* dst = smem + L::kPair + slot * L::kPairBytes + half * kBN * 128;
+                        if (p.pair_per_head)   // [B·H][KL][QL]: queries qt·128 + half·64.., keys j·128..
+                            tma_load_3d(dst, &tm_pair, &bars[kPairFull + slot], qt * kBM + half * 64, j * kBN, bh_q);
+                        else                   // per-head tiles [B·H][QLp/128][KLp][128]
+                            tma_load_4d(dst, &tm_pair, &bars[kPairFull + slot], half * 64, j * kBN, qt, bh_q);
+                    }
+                    pair_issued = u + 1;
+                }
+                return true;
+            };
             int issued = 0;
-            for (int j = 0; j < n_kt; ++j) {
+            bool run = !PAIR || load_pairs(0);
+            for (int j = 0; run && j < n_kt; ++j) {
                 const int s = j % S;
                 if (j >= S && !wait(&bars[kKVEmpty + s], ((j / S) - 1) & 1, ab, 1)) break;
                 issued = j + 1;
@@ -199,19 +248,29 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 for (int e2 = 0; e2 < E / 64; ++e2)
                     tma_load_3d(smem + L::kV + s * L::kKVBytes + e2 * kBN * 128, &tm_v, &bars[kVFull + s], e2 * 64,
                                 j * kBN, bh_k);
+                if (PAIR && j + 1 < n_kt) run = load_pairs(j + 1);
             }
+            // copies still in flight land before the CTA exits
             wait(&bars[kQFull], 0, ab, 2);
             for (int j = issued - S < 0 ? 0 : issued - S; j < issued; ++j) {
                 wait(&bars[kKFull + j % S], (j / S) & 1, ab, 3);
                 wait(&bars[kVFull + j % S], (j / S) & 1, ab, 3);
             }
+            for (int u = pair_issued - kPairSlots < 0 ? 0 : pair_issued - kPairSlots; u < pair_issued; ++u)
+                wait(&bars[kPairFull + u % kPairSlots], (u / kPairSlots) & 1, ab, 14);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         constexpr uint32_t idesc_s = idesc_f16<kBF16>(kBM, kBN, false, false);
         constexpr uint32_t idesc_o = idesc_f16<kBF16>(kBM, E, false, true);
         bool ok = n_kt > 0 && wait_warp(&bars[kQFull], 0, ab, 4);
-        auto issue_s = [&](int t, int j) {   // S_t(j) = Q_t·K_jᵀ, lane 0
+        const uint32_t sEye = smem_u32(smem + L::kEye);
+        int u_pair = 0;   // pair tiles consumed, in the producer's order
+        // the pair tile of the next score MMA has landed (warp-uniform)
+        auto pair_ready = [&]() -> bool {
+            return !PAIR || wait_warp(&bars[kPairFull + u_pair % kPairSlots], (u_pair / kPairSlots) & 1, ab, 15);
+        };
+        auto issue_s = [&](int t, int j) {   // S_t(j) = Q_t·K_jᵀ (+ c·I·pairᵀ), lane 0
             const int s = j % S;
             const uint32_t sQ = smem_u32(smem + L::kQ + t * L::kQBytes);
             const uint32_t sK = smem_u32(smem + L::kK + s * L::kKVBytes);
@@ -221,15 +280,26 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 const uint32_t off_k = (kk / 4) * kBN * 128 + (kk % 4) * 32;
                 umma_ss(tmem + t * W, desc_k_sw128(sQ + off_q), desc_k_sw128(sK + off_k), idesc_s, kk > 0 ? 1u : 0u);
             }
+            if (PAIR) {
+                // B = pair tile [key][query], K-major over queries
+                const int slot = u_pair % kPairSlots;
+                const uint32_t sP = smem_u32(smem + L::kPair + slot * L::kPairBytes);
+#pragma unroll
+                for (int kk = 0; kk < kBM / 16; ++kk)
+                    umma_ss(tmem + t * W, desc_k_sw128(eye_step(sEye, kk)),
+                            desc_k_sw128(sP + (kk / 4) * kBN * 128 + (kk % 4) * 32), idesc_s, 1u);
+                umma_commit(&bars[kPairEmpty + slot]);
+            }
             umma_commit(&bars[kSFull + t]);
         };
         if (ok) ok = wait_warp(&bars[kKFull], 0, ab, 5);
-        if (ok) {
+        for (int t = 0; ok && t < 2; ++t) {
+            if ((t ? nkt1 : nkt0) == 0) continue;
+            if (!pair_ready()) { ok = false; break; }
             tc_fence_after();
-            if (lane == 0)
-                for (int t = 0; t < 2; ++t)
-                    if ((t ? nkt1 : nkt0) > 0) issue_s(t, 0);
+            if (lane == 0) issue_s(t, 0);
             __syncwarp();
+            if (PAIR) ++u_pair;
         }
         for (int j = 0; ok && j < n_kt; ++j) {
             const int s = j % S;
@@ -240,6 +310,8 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 const int nk_t = t ? nkt1 : nkt0;
                 if (j >= nk_t) continue;
                 if (!wait_warp(&bars[kPFull + t], j & 1, ab, 8)) { ok = false; break; }
+                const bool more = j + 1 < nk_t;
+                if (more && !pair_ready()) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t sV = smem_u32(smem + L::kV + s * L::kKVBytes);
@@ -248,10 +320,11 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                         umma_ts(tmem + t * W + kBN, tmem + t * W + kk * 8, desc_mn_sw128(sV + kk * 16 * 128, kBN * 128),
                                 idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                     umma_commit(&bars[kOStep + t]);
-                    if (j == nk_t - 1) umma_commit(&bars[kOFinal + t]);
+                    if (!more) umma_commit(&bars[kOFinal + t]);
                     else issue_s(t, j + 1);   // behind PV_t(j), which reads P_t(j) from the same columns
                 }
                 __syncwarp();
+                if (PAIR && more) ++u_pair;
             }
             if (!ok) break;
             if (lane == 0) umma_commit(&bars[kKVEmpty + s]);   // K_j, V_j read by every MMA issued so far
@@ -390,29 +463,42 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     }
 }
 
-template <typename T, int E, bool CAUSAL, bool MASK>
-int launch2(const Params& p, cudaStream_t s) {
-    using Lay = Layout2<E>;
+template <typename T, int E, bool CAUSAL, bool PAIR, bool MASK>
+int launch2(const Params& p, const void* pair_tiles, cudaStream_t s) {
+    using Lay = Layout2<E, PAIR>;
     constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-    CUtensorMap tq, tk, tv;
+    const int64_t qlp = (p.QL + 127) / 128 * 128, klp = (p.KL + 127) / 128 * 128;
+    CUtensorMap tq, tk, tv, tp;
+    memset(&tp, 0, sizeof(tp));
     if (!make_map(&tq, p.q, E, p.QL, (int64_t)p.B * p.QH, kBM, bf16) ||
         !make_map(&tk, p.k, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
-        !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16))
+        !make_map(&tv, p.v, E, p.KL, (int64_t)p.B * p.KH, kBN, bf16) ||
+        (PAIR && !(p.pair_per_head ? make_per_head_map(&tp, p.pair, p.QL, p.KL, (int64_t)p.B * p.QH, bf16)
+                                   : make_tiles_map(&tp, pair_tiles, qlp, klp, (int64_t)p.B * p.QH, bf16))))
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cuTensorMapEncodeTiled failed");
-    auto kern = fa_fwd2_sm100_kernel<T, E, CAUSAL, MASK>;
+    auto kern = fa_fwd2_sm100_kernel<T, E, CAUSAL, PAIR, MASK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc) != cudaSuccess)
         return fail(NNOP_ERR_CUDA, "flash_attention_fwd: cannot set shared memory size");
     const int n_qt = (int)((p.QL + kBM - 1) / kBM);
     dim3 grid(p.QH, (unsigned)((n_qt + 1) / 2), p.B);
-    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, p);
+    kern<<<grid, kThreads, Lay::kAlloc, s>>>(tq, tk, tv, tp, p);
     return check_launch("flash_attention_fwd (sm100, two tiles)");
 }
 
+template <typename T, int E, bool CAUSAL>
+int dispatch2_flags(const Params& p, const void* pair_tiles, cudaStream_t s) {
+    const bool pair = p.pair != nullptr, mask = p.kmask != nullptr;
+    if constexpr (E == 64) {
+        if (pair) return mask ? launch2<T, 64, CAUSAL, true, true>(p, pair_tiles, s)
+                              : launch2<T, 64, CAUSAL, true, false>(p, pair_tiles, s);
+    }
+    return mask ? launch2<T, E, CAUSAL, false, true>(p, pair_tiles, s)
+                : launch2<T, E, CAUSAL, false, false>(p, pair_tiles, s);
+}
+
 template <typename T, int E>
-int dispatch2(const Params& p, bool causal, cudaStream_t s) {
-    const bool mask = p.kmask != nullptr;
-    if (causal) return mask ? launch2<T, E, true, true>(p, s) : launch2<T, E, true, false>(p, s);
-    return mask ? launch2<T, E, false, true>(p, s) : launch2<T, E, false, false>(p, s);
+int dispatch2(const Params& p, const void* pair_tiles, bool causal, cudaStream_t s) {
+    return causal ? dispatch2_flags<T, E, true>(p, pair_tiles, s) : dispatch2_flags<T, E, false>(p, pair_tiles, s);
 }
 
 }  // namespace
@@ -425,11 +511,14 @@ int sm100_fwd2_timeouts() {
     return v;
 }
 
-// The no-pair forward (bf16/f16, E 64 or 128).
-int sm100_fwd2(const Params& p, int dtype, bool causal, cudaStream_t s) {
+// The forward for bf16/f16, E 64 or 128; with a pair bias E = 64 only, the
+// bias from the per-head tiles (pair_tiles) or, with p.pair_per_head, from
+// the caller's per-head buffer.
+int sm100_fwd2(const Params& p, const void* pair_tiles, int dtype, bool causal, cudaStream_t s) {
     if (dtype == NNOP_BF16)
-        return p.E == 64 ? dispatch2<__nv_bfloat16, 64>(p, causal, s) : dispatch2<__nv_bfloat16, 128>(p, causal, s);
-    return p.E == 64 ? dispatch2<__half, 64>(p, causal, s) : dispatch2<__half, 128>(p, causal, s);
+        return p.E == 64 ? dispatch2<__nv_bfloat16, 64>(p, pair_tiles, causal, s)
+                         : dispatch2<__nv_bfloat16, 128>(p, pair_tiles, causal, s);
+    return p.E == 64 ? dispatch2<__half, 64>(p, pair_tiles, causal, s) : dispatch2<__half, 128>(p, pair_tiles, causal, s);
 }
 
 }  // namespace fa

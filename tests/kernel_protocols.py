@@ -587,21 +587,29 @@ def backward128(T: int, seed: int, plant: str | None = None, slow_tma: bool = Fa
     sim.run(roles)
 
 
-# ------------------------------------------------------------------ forward, two tiles (no pair)
+# ------------------------------------------------------------------ forward, two tiles
 def forward2(nkt0: int, nkt1: int, seed: int, stages: int = 2, rescale_p: float = 0.5,
-             plant: str | None = None, slow_tma: bool = False):
+             plant: str | None = None, slow_tma: bool = False, pair: bool = False):
     """fa_fwd2_sm100_kernel: two query tiles per CTA, one S buffer and one O
     accumulator per tile, one K/V ring both tiles read.  Per key tile j the MMA
     warp waits V_j (and K_{j+1}), then per tile t: PFull_t(j) -> PV_t(j),
     OStep_t, and S_t(j+1) behind it (same TMEM columns as P_t(j)) or OFinal_t;
     KVEmpty_j once both tiles' MMAs of step j are issued.  With a causal mask
-    the second tile has one key tile more (nkt1 = nkt0 + 1)."""
+    the second tile has one key tile more (nkt1 = nkt0 + 1).  With a pair bias
+    the pair tiles of (tile t, key tile j) go through one 3-slot ring in score
+    order (j major, t minor): the producer loads those of key tile j + 1 after
+    K/V_j, the u-th into slot u % 3 once PairEmpty says the score MMA of tile
+    u - 3 retired; the MMA warp waits PairFull before each score."""
     sim = _Sim(seed, slow_tma)
     S = stages
     nkt = [nkt0, nkt1]
     n_kt = max(nkt)
+    order = [(t, j) for j in range(n_kt) for t in range(2) if j < nkt[t]]   # pair tile u
     sim.bar("QFull")
     sim.bar("MmaDone")
+    for slot in range(3):
+        sim.bar(f"PairFull{slot}")
+        sim.bar(f"PairEmpty{slot}")
     for s in range(S):
         for n in ("KFull", "VFull", "KVEmpty"):
             sim.bar(f"{n}{s}")
@@ -615,6 +623,25 @@ def forward2(nkt0: int, nkt1: int, seed: int, stages: int = 2, rescale_p: float 
         if n_kt == 0:
             return
         sim.asyncs.append((lambda: sim.mem.__setitem__("Q", "q"), "QFull"))
+        issued = {"u": 0}
+
+        def load_pairs(j):
+            for t in range(2):
+                if j >= nkt[t]:
+                    continue
+                u = issued["u"]
+                slot = u % 3
+                if u >= 3:
+                    yield _wait(plant, f"PairEmpty{slot}", u // 3 - 1)
+
+                def land(u=u, slot=slot):
+                    if u >= 3 and ("S",) + order[u - 3] not in sim.executed:
+                        raise ProtocolBug(f"pair slot {slot} reloaded before S{order[u - 3]} read it")
+                    sim.mem[f"pair{slot}"] = order[u]
+                sim.asyncs.append((land, f"PairFull{slot}"))
+                issued["u"] = u + 1
+        if pair:
+            yield from load_pairs(0)
         for j in range(n_kt):
             s = j % S
             if j >= S:
@@ -631,26 +658,42 @@ def forward2(nkt0: int, nkt1: int, seed: int, stages: int = 2, rescale_p: float 
                 sim.mem[f"V{s}"] = j
             sim.asyncs.append((land_k, f"KFull{s}"))
             sim.asyncs.append((land_v, f"VFull{s}"))
+            if pair and j + 1 < n_kt:
+                yield from load_pairs(j + 1)
 
     def mma():
         if n_kt == 0:
             yield ("do", lambda: None)
             return
         yield ("wait", "QFull", 0)
+        used = {"u": 0}
+
+        def pair_ready():
+            if pair:
+                u = used["u"]
+                yield _wait(plant, f"PairFull{u % 3}", u // 3)
 
         def issue_s(t, j):
-            def run(t=t, j=j):
+            u = used["u"]
+
+            def run(t=t, j=j, u=u):
                 sim.expect("Q", "q")
                 sim.expect(f"K{j % S}", j)
+                if pair:
+                    sim.expect(f"pair{u % 3}", (t, j))
                 if j > 0 and ("PV", t, j - 1) not in sim.executed:
                     raise ProtocolBug(f"S_{t}({j}) overwrites P_{t}({j - 1}) before PV read it")
                 sim.mem[f"S{t}"] = ("S", j)
             sim.mma(("S", t, j), run)
+            if pair:
+                sim.commit(f"PairEmpty{u % 3}")
+                used["u"] = u + 1
             sim.commit(f"SFull{t}")
 
         yield _wait(plant, "KFull0", 0)
         for t in range(2):
             if nkt[t] > 0:
+                yield from pair_ready()
                 issue_s(t, 0)
         for j in range(n_kt):
             s = j % S
@@ -661,6 +704,8 @@ def forward2(nkt0: int, nkt1: int, seed: int, stages: int = 2, rescale_p: float 
                 if j >= nkt[t]:
                     continue
                 yield _wait(plant, f"PFull{t}", j)
+                if j + 1 < nkt[t]:
+                    yield from pair_ready()
 
                 def pv(t=t, j=j, s=s):
                     sim.expect(f"S{t}", ("P", j))

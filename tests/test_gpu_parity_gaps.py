@@ -2,6 +2,8 @@
 
 * the mma.sync kernel family (fa_mma.cu), selected for every shape by
   NNOP_B200_FA=mma: the E = 64 pair-bias cases, GQA and E = 128;
+* the one-tile tcgen05 forward (fa_fwd_sm100.cu), selected by
+  NNOP_B200_FA=one_tile;
 * the C-ABI forward called with a NULL workspace (the pair bias is then read
   in the reference layout by the mma.sync forward) followed by the tcgen05
   backward, which rebuilds the per-head pair tiles itself;
@@ -48,6 +50,20 @@ def test_mma_family_gqa_and_e128(monkeypatch, dtype):
                                    (2, 2, 200, 128, False)]:
         got, want = run_case(2, QH, KH, L, L, E, dtype, causal, False, False, seed=L + E)
         check(got, want, dtype, tag=f"mma E={E} L={L}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_one_tile_forward_family(monkeypatch, dtype):
+    """NNOP_B200_FA=one_tile: the one-query-tile tcgen05 forward
+    (fa_fwd_sm100.cu) that the two-tile kernel replaced by default, on pair,
+    mask, GQA and E = 128 cases."""
+    monkeypatch.setenv("NNOP_B200_FA", "one_tile")
+    for (B, QH, KH, QL, KL, E, causal, pair, use_mask) in [(2, 4, 4, 300, 421, 64, False, True, True),
+                                                           (1, 4, 4, 384, 384, 64, True, True, False),
+                                                           (2, 8, 2, 257, 257, 128, True, False, True),
+                                                           (1, 2, 1, 200, 77, 64, False, False, False)]:
+        got, want = run_case(B, QH, KH, QL, KL, E, dtype, causal, pair, use_mask, seed=QL + E)
+        check(got, want, dtype, tag=f"one_tile E={E} QL={QL} KL={KL} pair={pair}")
 
 
 def test_c_abi_forward_without_workspace():

@@ -66,12 +66,12 @@ def test_backward128_planted_mistake_is_caught(plant):
     assert _caught(kp.backward128, plant, T=7) or _caught(kp.backward128, plant, T=7, slow_tma=True)
 
 
-@pytest.mark.parametrize("stages", [2, 3])
+@pytest.mark.parametrize("stages,pair", [(2, False), (3, False), (2, True)])
 @pytest.mark.parametrize("slow_tma", [False, True])
-def test_forward2_protocol(stages, slow_tma):
-    for nkt0, nkt1 in [(0, 0), (1, 0), (1, 1), (1, 2), (3, 3), (4, 5), (6, 6), (2, 3)]:
+def test_forward2_protocol(stages, pair, slow_tma):
+    for nkt0, nkt1 in [(0, 0), (1, 0), (1, 1), (1, 2), (3, 3), (4, 5), (6, 6), (2, 3), (5, 0)]:
         for seed in range(30):
-            kp.forward2(nkt0, nkt1, seed, stages=stages, slow_tma=slow_tma)
+            kp.forward2(nkt0, nkt1, seed, stages=stages, slow_tma=slow_tma, pair=pair)
 
 
 @pytest.mark.parametrize("plant", ["KVEmpty0", "KVEmpty1", "KFull1", "VFull0", "PFull0", "PFull1", "SFull1",
@@ -79,6 +79,13 @@ def test_forward2_protocol(stages, slow_tma):
 def test_forward2_planted_mistake_is_caught(plant):
     assert (_caught(kp.forward2, plant, nkt0=4, nkt1=5) or
             _caught(kp.forward2, plant, nkt0=4, nkt1=5, slow_tma=True))
+
+
+@pytest.mark.parametrize("plant", ["PairFull0", "PairFull1", "PairFull2", "PairEmpty0", "PairEmpty1",
+                                   "PairEmpty2"])
+def test_forward2_pair_planted_mistake_is_caught(plant):
+    assert (_caught(kp.forward2, plant, nkt0=4, nkt1=5, pair=True) or
+            _caught(kp.forward2, plant, nkt0=4, nkt1=5, pair=True, slow_tma=True))
 
 
 def test_forward2_rescale_wait_is_implied():
