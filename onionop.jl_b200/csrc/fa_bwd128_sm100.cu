@@ -196,17 +196,23 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
         auto sQ = [&](int t) { return smem_u32(smem + Lay::kQ + (t % kStages) * Lay::kStep); };
         auto sDO = [&](int t) { return smem_u32(smem + Lay::kDO + (t % kStages) * Lay::kStep); };
+        // operand descriptors, built once and stepped with desc_add
+        const uint64_t dKk = desc_k_sw128(sK), dVk = desc_k_sw128(sV);
+        const uint64_t dQk = desc_k_sw128(sQ(0)), dDOk = desc_k_sw128(sDO(0));
+        const uint64_t dQmn = desc_mn_sw128(sQ(0), Lay::kStep / 2), dDOmn = desc_mn_sw128(sDO(0), Lay::kStep / 2);
+        const uint64_t dKmn = desc_mn_sw128(sK, Lay::kKV / 2);
+        const uint64_t dDSmn = desc_mn_sw128(smem_u32(smem + Lay::kDS), 0);
         // K-major SW128 operands stored as two 64-column boxes: K16 step kk of E
-        auto kmaj = [](uint32_t base, int box_bytes, int kk) {
-            return desc_k_sw128(base + (kk >> 2) * box_bytes + (kk & 3) * 32);
-        };
+        auto kmaj = [](int box_bytes, int kk) { return (uint32_t)((kk >> 2) * box_bytes + (kk & 3) * 32); };
         auto issue_score = [&](int t, bool dp) {   // Sᵀ (or dPᵀ) of step t, lane 0 only
             const int w = t & 1;
             const uint32_t d = tmem + 256 + 128 * w + (dp ? 64 : 0);
-            const uint32_t a = dp ? sV : sK, bq = dp ? sDO(t) : sQ(t);
+            const uint64_t a = dp ? dVk : dKk;
+            const uint64_t bq = desc_add(dp ? dDOk : dQk, (uint32_t)(t % kStages) * Lay::kStep);
 #pragma unroll
             for (int kk = 0; kk < kE / 16; ++kk)
-                umma_ss(d, kmaj(a, Lay::kKV / 2, kk), kmaj(bq, Lay::kStep / 2, kk), id_s, kk > 0 ? 1u : 0u);
+                umma_ss(d, desc_add(a, kmaj(Lay::kKV / 2, kk)), desc_add(bq, kmaj(Lay::kStep / 2, kk)), id_s,
+                        kk > 0 ? 1u : 0u);
         };
         bool ok = steps > 0 && wait_warp(&bars[kKVFull], 0, ab, 2);
         for (int t = 0; ok && t < 2 && t < steps; ++t) {
@@ -226,20 +232,21 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
             tc_fence_after();
             if (lane == 0) {
                 // products of step t: Pᵀ / dSᵀ of query chunk kk at Sᵀ columns 16kk / 16kk + 8
+                const uint32_t qoff = (uint32_t)(t % kStages) * Lay::kStep;
+                const uint64_t bdo = desc_add(dDOmn, qoff), bq = desc_add(dQmn, qoff);
+                const uint32_t acc0 = t > 0 ? 1u : 0u;
 #pragma unroll
                 for (int kk = 0; kk < kSM / 16; ++kk) {
-                    const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-                    umma_ts(tDV, tSw + 16 * kk, desc_mn_sw128(sDO(t) + kk * 16 * 128, Lay::kStep / 2), id_kv, acc);
-                    umma_ts(tDK, tSw + 16 * kk + 8, desc_mn_sw128(sQ(t) + kk * 16 * 128, Lay::kStep / 2), id_kv,
-                            acc);
+                    const uint32_t acc = kk > 0 ? 1u : acc0;
+                    umma_ts(tDV, tSw + 16 * kk, desc_add(bdo, kk * 16 * 128), id_kv, acc);
+                    umma_ts(tDK, tSw + 16 * kk + 8, desc_add(bq, kk * 16 * 128), id_kv, acc);
                 }
                 umma_commit(&bars[kQEmpty + t % kStages]);
                 // dQᵀ = Kᵀ·dSᵀ into the warpgroup's dPᵀ columns (read out by the elementwise step)
-                const uint32_t sDS = smem_u32(smem + Lay::kDS + w * Lay::kDSBytes);
+                const uint64_t bds = desc_add(dDSmn, (uint32_t)w * Lay::kDSBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk)
-                    umma_ss(tDPw, desc_mn_sw128(sK + kk * 16 * 128, Lay::kKV / 2), desc_mn_sw128(sDS + kk * 16 * 128, 0),
-                            id_q, kk > 0 ? 1u : 0u);
+                    umma_ss(tDPw, desc_add(dKmn, kk * 16 * 128), desc_add(bds, kk * 16 * 128), id_q, kk > 0 ? 1u : 0u);
                 umma_commit(&bars[kDQFull + w]);
             }
             __syncwarp();

@@ -214,6 +214,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t id_kv = idesc_f16<kBF16>(128, kE, false, true);    // dV, dK (A in TMEM)
         constexpr uint32_t id_q = idesc_f16<kBF16>(128, kE, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
+        const uint64_t dK = desc_k_sw128(sK), dV = desc_k_sw128(sV), dKmn = desc_mn_sw128(sK, 0);
+        const uint64_t dQk = desc_k_sw128(smem_u32(smem + Lay::kQ)), dDOk = desc_k_sw128(smem_u32(smem + Lay::kDO));
+        const uint64_t dQmn = desc_mn_sw128(smem_u32(smem + Lay::kQ), 0), dDOmn = desc_mn_sw128(smem_u32(smem + Lay::kDO), 0);
+        const uint64_t dDSmn = desc_mn_sw128(smem_u32(smem + Lay::kDS), kBN * 128);
         // Sᵀ/dPᵀ of half hf of tile t into the half's TMEM buffers
         auto issue_s = [&](int t, int hf) -> bool {
             const int s = t & 1;
@@ -222,13 +226,13 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tc_fence_after();
             }
             if (lane == 0) {
-                const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile) + hf * kHM * 128;
-                const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile) + hf * kHM * 128;
+                const uint32_t off = (uint32_t)(s * Lay::kTile + hf * kHM * 128);
+                const uint64_t bq = desc_add(dQk, off), bdo = desc_add(dDOk, off);
                 const uint32_t dS = tS + hf * kHM, dDP = tDP + hf * kHM;
 #pragma unroll
                 for (int kk = 0; kk < kE / 16; ++kk) {
-                    umma_ss(dS, desc_k_sw128(sK + kk * 32), desc_k_sw128(sQ + kk * 32), id_s, kk > 0 ? 1u : 0u);
-                    umma_ss(dDP, desc_k_sw128(sV + kk * 32), desc_k_sw128(sDO + kk * 32), id_s, kk > 0 ? 1u : 0u);
+                    umma_ss(dS, desc_add(dK, kk * 32), desc_add(bq, kk * 32), id_s, kk > 0 ? 1u : 0u);
+                    umma_ss(dDP, desc_add(dV, kk * 32), desc_add(bdo, kk * 32), id_s, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&bars[kSFull + hf]);
             }
@@ -257,15 +261,16 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     bulk_wait_read<2>();
                 }
                 if (lane == 0) {
-                    const uint32_t sQ = smem_u32(smem + Lay::kQ + s * Lay::kTile) + hf * kHM * 128;
-                    const uint32_t sDO = smem_u32(smem + Lay::kDO + s * Lay::kTile) + hf * kHM * 128;
+                    const uint32_t off = (uint32_t)(s * Lay::kTile + hf * kHM * 128);
+                    const uint64_t bq = desc_add(dQmn, off), bdo = desc_add(dDOmn, off);
+                    const uint32_t acc0 = (t > 0 || hf > 0) ? 1u : 0u;
 #pragma unroll
                     for (int kk = 0; kk < kHM / 16; ++kk) {
                         // packed 16-bit Pᵀ/dSᵀ of the half's queries [16kk, 16kk+16)
                         const uint32_t pcol = hf * kHM + kk * 8;
-                        const uint32_t acc = (t > 0 || hf > 0 || kk > 0) ? 1u : 0u;
-                        umma_ts(tDV, tS + pcol, desc_mn_sw128(sDO + kk * 16 * 128, 0), id_kv, acc);
-                        umma_ts(tDK, tDP + pcol, desc_mn_sw128(sQ + kk * 16 * 128, 0), id_kv, acc);
+                        const uint32_t acc = kk > 0 ? 1u : acc0;
+                        umma_ts(tDV, tS + pcol, desc_add(bdo, kk * 16 * 128), id_kv, acc);
+                        umma_ts(tDK, tDP + pcol, desc_add(bq, kk * 16 * 128), id_kv, acc);
                     }
                     if (hf == 1) umma_commit(&bars[kQEmpty + s]);
                 }
@@ -277,11 +282,10 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             if (t > 0 && !wait_warp(&bars[kDQEmpty], (t - 1) & 1, ab, 7)) break;
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t sDS = smem_u32(smem + Lay::kDS + s * Lay::kDSBytes);
+                const uint64_t bds = desc_add(dDSmn, (uint32_t)s * Lay::kDSBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk)
-                    umma_ss(tDQ, desc_mn_sw128(sDS + kk * 16 * 128, kBN * 128), desc_mn_sw128(sK + kk * 16 * 128, 0),
-                            id_q, kk > 0 ? 1u : 0u);
+                    umma_ss(tDQ, desc_add(bds, kk * 16 * 128), desc_add(dKmn, kk * 16 * 128), id_q, kk > 0 ? 1u : 0u);
                 // the dQ warps reuse this dS buffer as staging once dQ_t is
                 // done: the dS stores must have read it by then
                 if (PAIR) bulk_wait_read<0>();

@@ -270,24 +270,27 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         auto pair_ready = [&]() -> bool {
             return !PAIR || wait_warp(&bars[kPairFull + u_pair % kPairSlots], (u_pair / kPairSlots) & 1, ab, 15);
         };
+        // operand descriptors, built once and stepped with desc_add
+        const uint64_t dQ0 = desc_k_sw128(smem_u32(smem + L::kQ)), dK0 = desc_k_sw128(smem_u32(smem + L::kK));
+        const uint64_t dV0 = desc_mn_sw128(smem_u32(smem + L::kV), kBN * 128);
+        const uint64_t dEye = desc_k_sw128(sEye), dP0 = desc_k_sw128(smem_u32(smem + L::kPair));
         auto issue_s = [&](int t, int j) {   // S_t(j) = Q_t·K_jᵀ (+ c·I·pairᵀ), lane 0
-            const int s = j % S;
-            const uint32_t sQ = smem_u32(smem + L::kQ + t * L::kQBytes);
-            const uint32_t sK = smem_u32(smem + L::kK + s * L::kKVBytes);
+            const uint64_t bq = desc_add(dQ0, (uint32_t)t * L::kQBytes);
+            const uint64_t bk = desc_add(dK0, (uint32_t)(j % S) * L::kKVBytes);
 #pragma unroll
             for (int kk = 0; kk < E / 16; ++kk) {
                 const uint32_t off_q = (kk / 4) * kBM * 128 + (kk % 4) * 32;
                 const uint32_t off_k = (kk / 4) * kBN * 128 + (kk % 4) * 32;
-                umma_ss(tmem + t * W, desc_k_sw128(sQ + off_q), desc_k_sw128(sK + off_k), idesc_s, kk > 0 ? 1u : 0u);
+                umma_ss(tmem + t * W, desc_add(bq, off_q), desc_add(bk, off_k), idesc_s, kk > 0 ? 1u : 0u);
             }
             if (PAIR) {
                 // B = pair tile [key][query], K-major over queries
                 const int slot = u_pair % kPairSlots;
-                const uint32_t sP = smem_u32(smem + L::kPair + slot * L::kPairBytes);
+                const uint64_t bp = desc_add(dP0, (uint32_t)slot * L::kPairBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)
-                    umma_ss(tmem + t * W, desc_k_sw128(eye_step(sEye, kk)),
-                            desc_k_sw128(sP + (kk / 4) * kBN * 128 + (kk % 4) * 32), idesc_s, 1u);
+                    umma_ss(tmem + t * W, desc_add(dEye, eye_step(0, kk)),
+                            desc_add(bp, (kk / 4) * kBN * 128 + (kk % 4) * 32), idesc_s, 1u);
                 umma_commit(&bars[kPairEmpty + slot]);
             }
             umma_commit(&bars[kSFull + t]);
@@ -314,11 +317,12 @@ fa_fwd2_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 if (more && !pair_ready()) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t sV = smem_u32(smem + L::kV + s * L::kKVBytes);
+                    const uint64_t bv = desc_add(dV0, (uint32_t)s * L::kKVBytes);
+                    const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
                     for (int kk = 0; kk < kBN / 16; ++kk)
-                        umma_ts(tmem + t * W + kBN, tmem + t * W + kk * 8, desc_mn_sw128(sV + kk * 16 * 128, kBN * 128),
-                                idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                        umma_ts(tmem + t * W + kBN, tmem + t * W + kk * 8, desc_add(bv, kk * 16 * 128), idesc_o,
+                                kk > 0 ? 1u : acc0);
                     umma_commit(&bars[kOStep + t]);
                     if (!more) umma_commit(&bars[kOFinal + t]);
                     else issue_s(t, j + 1);   // behind PV_t(j), which reads P_t(j) from the same columns

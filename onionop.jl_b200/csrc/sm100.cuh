@@ -236,6 +236,14 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t addr) {
     d |= (uint64_t)2 << 61;                   // 128-byte swizzle
     return d;
 }
+// The descriptor of (descriptor d's start address + off bytes): the start
+// address is the low 14-bit field in 16-byte units, and every shared-memory
+// address (< 256 KB) fits it, so the offset never carries out of the field.
+// Issue loops build each operand's descriptor once and step it with this:
+// one 64-bit add per UMMA, where a rebuilt descriptor costs the issuing
+// thread several dependent instructions (measured: the single issuing thread,
+// not the tensor pipe, set the pace when every UMMA rebuilt its descriptors).
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off) { return d + (uint64_t)(off >> 4); }
 // MN-major operand in the 128-byte-swizzle canonical layout: 64 contiguous
 // MN elements per 128-byte row, consecutive K in consecutive rows, 8-row atoms
 // of 1024 B along K (stride byte offset), 64-element MN groups `lbo` bytes apart.
