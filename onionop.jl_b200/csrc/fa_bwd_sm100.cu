@@ -10,8 +10,8 @@
 // 64-query halves, half hf by elementwise warpgroup hf, each with its own
 // TMEM score buffers, so the tensor cores work on one half while the other
 // half's exponentials run.  Per tile t and half hf:
-//   Sᵀ  = K·Q_hfᵀ              (keys on TMEM lanes)     UMMA ss
-//   dPᵀ = V·dO_hfᵀ                                       UMMA ss
+//   Sᵀ  = K·Q_hfᵀ              (keys on TMEM lanes)     UMMA ts (K from TMEM)
+//   dPᵀ = V·dO_hfᵀ                                       UMMA ts (V from TMEM)
 //   Pᵀ  = exp(Sᵀ·scale + pairᵀ − lse),  dSᵀ = Pᵀ∘(dPᵀ − δ)   (elementwise)
 //   dV += Pᵀ·dO_hf   (Pᵀ from TMEM)                      UMMA ts
 //   dK += dSᵀ·Q_hf   (dSᵀ from TMEM)                     UMMA ts
@@ -38,10 +38,17 @@
 //   warps 12-15 dQ: TMEM dQ rows -> staged fp32 boxes -> TMA reduce-add;
 //               with a per-head dpair, warp 12 first writes its zeros
 // TMEM columns: Sᵀ half 0 [0,64), half 1 [64,128), dPᵀ half 0 [128,192),
-// half 1 [192,256), dV [256,320), dK [320,384), dQ [384,448).  The 16-bit
-// Pᵀ / dSᵀ of a half overwrite the first 32 columns of its own score buffers.
+// half 1 [192,256), dV [256,320), dK [320,384), dQ [384,448), K [448,480),
+// V [480,512) (16-bit pairs).  The 16-bit Pᵀ / dSᵀ of a half overwrite the
+// first 32 columns of its own score buffers.  K and V, constant for the whole
+// walk, are copied into TMEM once (the elementwise threads move their key's
+// row from the TMA-loaded shared tile) so the score MMAs read only Q / dO from
+// shared memory: an N = 64 UMMA with both operands in shared memory needs the
+// full shared-memory bandwidth (6 KB per 48 cycles) and slows down with every
+// other shared-memory user (TMA fills, dS and dQ staging, pair reads); with A
+// from TMEM it reads 2 KB.
 // All mbarrier waits are bounded; a wait that gives up records its site
-// (0-14) in the timeout flags and the CTA leaves.
+// (0-16) in the timeout flags and the CTA leaves.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -77,7 +84,8 @@ enum Bar {
     kFinal = 17,      // every MMA retired
     kPairFull = 18,   // +slot: pair half tile landed (TMA)
     kPairEmpty = 21,  // +slot: its warpgroup is done with it (128 arrivals)
-    kNumBars = 24
+    kKVTmem = 24,     // K and V copied into TMEM (256 arrivals)
+    kNumBars = 25
 };
 
 struct Lay {
@@ -131,6 +139,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     if (threadIdx.x == 0) {
         s_abort = 0;
         mbar_init(&bars[kKVFull], 1);
+        mbar_init(&bars[kKVTmem], 256);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars[kQFull + s], 1);
             mbar_init(&bars[kQEmpty + s], 1);
@@ -158,6 +167,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
+    const uint32_t tK = tmem + 448, tV = tmem + 480;
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
@@ -214,7 +224,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         constexpr uint32_t id_kv = idesc_f16<kBF16>(128, kE, false, true);    // dV, dK (A in TMEM)
         constexpr uint32_t id_q = idesc_f16<kBF16>(128, kE, true, true);      // dQ (A = dS, MN-major)
         const uint32_t sK = smem_u32(smem + Lay::kK), sV = smem_u32(smem + Lay::kV);
-        const uint64_t dK = desc_k_sw128(sK), dV = desc_k_sw128(sV), dKmn = desc_mn_sw128(sK, 0);
+        const uint64_t dKmn = desc_mn_sw128(sK, 0);
         const uint64_t dQk = desc_k_sw128(smem_u32(smem + Lay::kQ)), dDOk = desc_k_sw128(smem_u32(smem + Lay::kDO));
         const uint64_t dQmn = desc_mn_sw128(smem_u32(smem + Lay::kQ), 0), dDOmn = desc_mn_sw128(smem_u32(smem + Lay::kDO), 0);
         const uint64_t dDSmn = desc_mn_sw128(smem_u32(smem + Lay::kDS), kBN * 128);
@@ -231,15 +241,15 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 const uint32_t dS = tS + hf * kHM, dDP = tDP + hf * kHM;
 #pragma unroll
                 for (int kk = 0; kk < kE / 16; ++kk) {
-                    umma_ss(dS, desc_add(dK, kk * 32), desc_add(bq, kk * 32), id_s, kk > 0 ? 1u : 0u);
-                    umma_ss(dDP, desc_add(dV, kk * 32), desc_add(bdo, kk * 32), id_s, kk > 0 ? 1u : 0u);
+                    umma_ts(dS, tK + kk * 8, desc_add(bq, kk * 32), id_s, kk > 0 ? 1u : 0u);
+                    umma_ts(dDP, tV + kk * 8, desc_add(bdo, kk * 32), id_s, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&bars[kSFull + hf]);
             }
             __syncwarp();
             return true;
         };
-        bool ok = tiles > 0 && wait_warp(&bars[kKVFull], 0, ab, 3);
+        bool ok = tiles > 0 && wait_warp(&bars[kKVFull], 0, ab, 3) && wait_warp(&bars[kKVTmem], 0, ab, 15);
         if (ok) ok = issue_s(0, 0) && issue_s(0, 1);
         for (int t = 0; ok && t < tiles; ++t) {
             const int s = t & 1;
@@ -325,6 +335,21 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tSh = tS + hf * kHM + lane_off, tDPh = tDP + hf * kHM + lane_off;
         const float sl2 = p.scale * kLog2e;
+        if (tiles > 0 && wait_warp(&bars[kKVFull], 0, ab, 16)) {
+            // this key's row of K (half-0 warpgroup) or V (half 1) into TMEM as
+            // 16-bit pairs, the A operand of the score MMAs
+            const uint8_t* row = smem + (hf ? Lay::kV : Lay::kK) + jr * 128;
+            uint32_t kr[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint4 u = *reinterpret_cast<const uint4*>(row + ((c ^ (jr & 7)) << 4));
+                kr[4 * c] = u.x; kr[4 * c + 1] = u.y; kr[4 * c + 2] = u.z; kr[4 * c + 3] = u.w;
+            }
+            tmem_st32((hf ? tV : tK) + lane_off, kr);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&bars[kKVTmem]);
+        }
         for (int t = 0; t < tiles; ++t) {
             const int buf = t & 1;
             const int64_t qh0 = (int64_t)(qt0 + t % nq) * kBM + hf * kHM;   // first query of the half

@@ -36,11 +36,13 @@ class _Bar:
 
 
 class _Sim:
-    def __init__(self, seed, slow_tma: bool = False):
+    def __init__(self, seed, slow_tma: bool = False, slow_roles=()):
         # slow_tma: a copy in flight lands only rarely while anything else can
         # run (long TMA latencies), which exposes waits on copies that the
-        # uniform schedule would nearly always find already landed.
+        # uniform schedule would nearly always find already landed; roles in
+        # slow_roles likewise run only rarely while anything else can.
         self.slow_tma = slow_tma
+        self.slow_roles = set(slow_roles)
         self.rng = random.Random(seed)
         self.bars, self.mem, self.pipe, self.asyncs = {}, {}, [], []
         self.executed = set()
@@ -85,6 +87,10 @@ class _Sim:
                 raise ProtocolBug(f"deadlock: {[(n, blocked[n]) for n in roles if n not in finished]}")
             if self.slow_tma and len(c) > 1 and c[-1][0] == "async" and self.rng.random() < 0.97:
                 c.pop()
+            if self.slow_roles and self.rng.random() < 0.97:
+                fast = [x for x in c if not (x[0] == "role" and x[1] in self.slow_roles)]
+                if fast:
+                    c = fast
             kind, n = self.rng.choice(c)
             if kind == "pipe":
                 op = self.pipe.pop(0)
@@ -249,16 +255,18 @@ def forward(n_kt: int, pair: bool, seed: int, rescale_p: float = 0.5, plant: str
 
 
 # ------------------------------------------------------------------ backward (E = 64)
-def backward(T: int, pair: bool, seed: int, plant: str | None = None):
+def backward(T: int, pair: bool, seed: int, plant: str | None = None, slow_roles=()):
     """fa_bwd_sm100_kernel (E = 64): Q/dO 2-stage ring per 128-query tile; two
     64-query halves with their own TMEM Sᵀ/dPᵀ and elementwise warpgroups;
     products (dV, dK) per half, S(t+1, half) right behind them; per tile dQ
     from the tile's dS buffer (2 buffers), drained by 4 dQ warps that then
     stage fp32 rows in that buffer; with a pair bias the MMA warp TMA-stores
     each dS half (bulk_wait_read<2> per half, <0> before the dQ commit) and the
-    pair arrives in a 3-slot ring of half tiles."""
-    sim = _Sim(seed)
-    for n, c in (("KVFull", 1), ("DQFull", 1), ("DQEmpty", 4), ("Final", 1)):
+    pair arrives in a 3-slot ring of half tiles.  K and V go from their TMA
+    tile into TMEM (the score MMAs' A operand) by the elementwise threads once
+    KVFull completes; the MMA warp waits KVTmem before its first score."""
+    sim = _Sim(seed, slow_roles=slow_roles)
+    for n, c in (("KVFull", 1), ("KVTmem", 2), ("DQFull", 1), ("DQEmpty", 4), ("Final", 1)):
         sim.bar(n, c)
     for i in range(2):
         for n, c in (("QFull", 1), ("QEmpty", 1), ("SFull", 1), ("PFull", 1), ("DSEmpty", 4), ("TileFull", 1),
@@ -296,6 +304,7 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None):
 
     def mma():
         yield ("wait", "KVFull", 0)
+        yield _wait(plant, "KVTmem", 0)
         issued = []
 
         def issue_s(t, h):
@@ -303,6 +312,8 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None):
                 yield _wait(plant, f"QFull{t & 1}", t >> 1)
 
             def run(t=t, h=h):
+                sim.expect("KVT0", "kv")
+                sim.expect("KVT1", "kv")
                 sim.expect(f"Q{t & 1}", t)
                 if t > 0 and ("P", t - 1, h) not in sim.executed:
                     raise ProtocolBug(f"S({t},{h}) overwrites P/dS before products({t - 1},{h})")
@@ -367,6 +378,13 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None):
             yield ("arrive", f"TileFull{t & 1}")
 
     def elementwise(h):
+        yield _wait(plant, "KVFull", 0)
+
+        def to_tmem(h=h):
+            sim.expect("KV", "kv")
+            sim.mem[f"KVT{h}"] = "kv"
+        yield ("do", to_tmem)
+        yield ("arrive", "KVTmem")
         for t in range(T):
             yield _wait(plant, f"TileFull{t & 1}", t >> 1)
             yield _wait(plant, f"SFull{h}", t)
