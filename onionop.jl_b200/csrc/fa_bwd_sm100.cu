@@ -26,8 +26,9 @@
 // The pair bias is read in the elementwise step from the key-major per-head
 // copy pair_tiles() writes: each half tile [128 keys][64 queries] is one TMA
 // box (128-byte swizzle), so a thread reads its key's 16 queries as two
-// conflict-free 16-byte vectors.  Half tiles rotate through a 3-slot ring, so
-// the next tile's first half is in flight while the current one is read.
+// conflict-free 16-byte vectors.  Half tiles rotate through a 4-slot ring (the
+// fourth slot is V's shared tile, free once V is in TMEM), so the next tile's
+// halves are in flight while the current ones are read.
 // Warp roles (512 threads):
 //   warp 0      TMA producer (K, V once; Q_t, dO_t into a 2-stage ring; the
 //               pair half tiles of (query tile, key tile, head))
@@ -69,6 +70,7 @@ constexpr int kBM = 128;   // queries per tile
 constexpr int kHM = 64;    // queries per half
 constexpr int kE = 64;
 constexpr int kThreads = 512;
+constexpr int kPairSlots = 4;   // pair half tiles in flight: 3 slots + V's tile once V is in TMEM
 
 enum Bar {
     kKVFull = 0,
@@ -83,9 +85,9 @@ enum Bar {
     kTileEmpty = 15,  // +buffer: elementwise -> provider (256 arrivals)
     kFinal = 17,      // every MMA retired
     kPairFull = 18,   // +slot: pair half tile landed (TMA)
-    kPairEmpty = 21,  // +slot: its warpgroup is done with it (128 arrivals)
-    kKVTmem = 24,     // K and V copied into TMEM (256 arrivals)
-    kNumBars = 25
+    kPairEmpty = 22,  // +slot: its warpgroup is done with it (128 arrivals)
+    kKVTmem = 26,     // K and V copied into TMEM (256 arrivals)
+    kNumBars = 27
 };
 
 struct Lay {
@@ -152,7 +154,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_init(&bars[kDQFull], 1);
         mbar_init(&bars[kDQEmpty], 128);
         mbar_init(&bars[kFinal], 1);
-        for (int s = 0; s < 3; ++s) {
+        for (int s = 0; s < kPairSlots; ++s) {
             mbar_init(&bars[kPairFull + s], 1);
             mbar_init(&bars[kPairEmpty + s], 128);
         }
@@ -168,6 +170,35 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
     const uint32_t tK = tmem + 448, tV = tmem + 480;
+    // pair slot n: three slots of their own, the fourth is V's shared tile
+    // (free once V is in TMEM)
+    auto pair_slot = [&](int slot) { return smem + (slot < 3 ? Lay::kPair + slot * Lay::kPairSlot : Lay::kV); };
+    // pair half tile n = 2t + hf into slot n % 4 once half tile n - 4 is
+    // consumed; slot 3 (V's tile) only after V is in TMEM.  The producer
+    // issues them after each tile's Q/dO, in step with the tiles (a thread of
+    // its own running ahead measured no faster, and slower with the caller's
+    // per-head bias, whose scattered 128-byte rows compete with the dpair
+    // stores).  With that order the PairEmpty waits never wait: the products
+    // of tile t-2, which the QEmpty wait before tile t's loads follows, come
+    // after the elementwise reads of the slots' previous half tiles.
+    auto load_pair = [&](int n) -> bool {
+        const int slot = n % kPairSlots;
+        if (n >= kPairSlots && !wait(&bars[kPairEmpty + slot], ((n / kPairSlots) - 1) & 1, ab, 1)) return false;
+        if (n == 3 && !wait(&bars[kKVTmem], 0, ab, 1)) return false;
+        const int t = n >> 1, hf = n & 1;
+        const int h = kvh * p.n_rep + t / nq;
+        const int q0 = (qt0 + t % nq) * kBM;
+        mbar_expect_tx(&bars[kPairFull + slot], Lay::kPairSlot);
+        if (p.pair_per_head)   // [B·H][KL][QL]
+            tma_load_3d(pair_slot(slot), &tm_pair, &bars[kPairFull + slot], q0 + hf * kHM, (int)k0, b * QH + h);
+        else                   // per-head tiles [B·H][QLp/128][KLp][128]
+            tma_load_4d(pair_slot(slot), &tm_pair, &bars[kPairFull + slot], hf * kHM, (int)k0, q0 / kBM, b * QH + h);
+        return true;
+    };
+    auto drain_pairs = [&](int issued) {   // copies in flight land before the CTA leaves
+        for (int n = issued - kPairSlots < 0 ? 0 : issued - kPairSlots; n < issued; ++n)
+            wait(&bars[kPairFull + n % kPairSlots], (n / kPairSlots) & 1, ab, 2);
+    };
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
@@ -182,23 +213,6 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             tma_load_3d(smem + Lay::kK, &tm_k, &bars[kKVFull], 0, (int)k0, bh_k);
             tma_load_3d(smem + Lay::kV, &tm_v, &bars[kKVFull], 0, (int)k0, bh_k);
             int issued = 0, pair_issued = 0;
-            // pair half tile n = 2t + hf goes to slot n % 3 once half tile n - 3 is consumed
-            auto load_pair = [&](int n) -> bool {
-                const int slot = n % 3;
-                if (n >= 3 && !wait(&bars[kPairEmpty + slot], ((n / 3) - 1) & 1, ab, 1)) return false;
-                const int t = n >> 1, hf = n & 1;
-                const int h = kvh * p.n_rep + t / nq;
-                const int q0 = (qt0 + t % nq) * kBM;
-                mbar_expect_tx(&bars[kPairFull + slot], Lay::kPairSlot);
-                if (p.pair_per_head)   // [B·H][KL][QL]
-                    tma_load_3d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot],
-                                q0 + hf * kHM, (int)k0, b * QH + h);
-                else                   // per-head tiles [B·H][QLp/128][KLp][128]
-                    tma_load_4d(smem + Lay::kPair + slot * Lay::kPairSlot, &tm_pair, &bars[kPairFull + slot],
-                                hf * kHM, (int)k0, q0 / kBM, b * QH + h);
-                pair_issued = n + 1;
-                return true;
-            };
             bool run = true;
             for (int t = 0; run && t < tiles; ++t) {
                 const int s = t & 1;
@@ -209,14 +223,16 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                 tma_load_3d(smem + Lay::kQ + s * Lay::kTile, &tm_q, &bars[kQFull + s], 0, q0, b * QH + h);
                 tma_load_3d(smem + Lay::kDO + s * Lay::kTile, &tm_do, &bars[kQFull + s], 0, q0, b * QH + h);
                 issued = t + 1;
-                if (PAIR) run = load_pair(2 * t) && load_pair(2 * t + 1);
+                for (int hf = 0; PAIR && run && hf < 2; ++hf) {
+                    run = load_pair(2 * t + hf);
+                    if (run) pair_issued = 2 * t + hf + 1;
+                }
             }
             // copies in flight land before the CTA leaves (bounded waits)
             wait(&bars[kKVFull], 0, ab, 2);
             for (int t = issued - 2 < 0 ? 0 : issued - 2; t < issued; ++t)
                 wait(&bars[kQFull + (t & 1)], (t >> 1) & 1, ab, 2);
-            for (int n = pair_issued - 3 < 0 ? 0 : pair_issued - 3; n < pair_issued; ++n)
-                wait(&bars[kPairFull + n % 3], (n / 3) & 1, ab, 2);
+            if (PAIR) drain_pairs(pair_issued);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -318,10 +334,18 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const int h = kvh * p.n_rep + t / nq;
             const int64_t q0 = (int64_t)(qt0 + t % nq) * kBM;
             const int64_t ro = ((int64_t)b * QH + h) * QL;
-            for (int u = tp; u < kBM; u += 64) {
-                const int64_t i = q0 + u;
-                sLse[buf * kBM + u] = i < QL ? p.lse[ro + i] * kLog2e : 0.f;
-                sDel[buf * kBM + u] = i < QL ? p.delta[ro + i] : 0.f;
+            // both queries' loads in flight before the stores
+            float lv[kBM / 64], dv[kBM / 64];
+#pragma unroll
+            for (int r = 0; r < kBM / 64; ++r) {
+                const int64_t i = q0 + tp + 64 * r;
+                lv[r] = i < QL ? __ldg(p.lse + ro + i) : 0.f;
+                dv[r] = i < QL ? __ldg(p.delta + ro + i) : 0.f;
+            }
+#pragma unroll
+            for (int r = 0; r < kBM / 64; ++r) {
+                sLse[buf * kBM + tp + 64 * r] = lv[r] * kLog2e;
+                sDel[buf * kBM + tp + 64 * r] = dv[r];
             }
             mbar_arrive(&bars[kTileFull + buf]);
         }
@@ -356,8 +380,8 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             if (!wait_warp(&bars[kTileFull + buf], (t >> 1) & 1, ab, 10)) break;
             if (!wait_warp(&bars[kSFull + hf], t & 1, ab, 11)) break;
             if (t >= 2 && !wait_warp(&bars[kDSEmpty + buf], ((t >> 1) - 1) & 1, ab, 12)) break;
-            const int pn = 2 * t + hf, pslot = pn % 3;
-            if (PAIR && !wait_warp(&bars[kPairFull + pslot], (pn / 3) & 1, ab, 5)) break;
+            const int pn = 2 * t + hf, pslot = pn % kPairSlots;
+            if (PAIR && !wait_warp(&bars[kPairFull + pslot], (pn / kPairSlots) & 1, ab, 5)) break;
             tc_fence_after();
             // valid query columns of this key within the half: [cmin, cmax)
             const int64_t nvq = QL - qh0;
@@ -367,7 +391,7 @@ fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             uint8_t* sDS = smem + Lay::kDS + buf * Lay::kDSBytes + hf * (kBN * 128) + jr * 128;
             const float* lse_h = sLse + buf * kBM + hf * kHM;
             const float* del_h = sDel + buf * kBM + hf * kHM;
-            const uint8_t* prow = smem + Lay::kPair + pslot * Lay::kPairSlot + jr * 128;
+            const uint8_t* prow = pair_slot(pslot) + jr * 128;
 #pragma unroll 1
             for (int cc = 0; cc < kHM / 16; ++cc) {
                 const int col = cc * 16;

@@ -255,24 +255,27 @@ def forward(n_kt: int, pair: bool, seed: int, rescale_p: float = 0.5, plant: str
 
 
 # ------------------------------------------------------------------ backward (E = 64)
-def backward(T: int, pair: bool, seed: int, plant: str | None = None, slow_roles=()):
+def backward(T: int, pair: bool, seed: int, plant: str | None = None, slow_roles=(), slow_tma: bool = False):
     """fa_bwd_sm100_kernel (E = 64): Q/dO 2-stage ring per 128-query tile; two
     64-query halves with their own TMEM Sᵀ/dPᵀ and elementwise warpgroups;
     products (dV, dK) per half, S(t+1, half) right behind them; per tile dQ
     from the tile's dS buffer (2 buffers), drained by 4 dQ warps that then
     stage fp32 rows in that buffer; with a pair bias the MMA warp TMA-stores
     each dS half (bulk_wait_read<2> per half, <0> before the dQ commit) and the
-    pair arrives in a 3-slot ring of half tiles.  K and V go from their TMA
+    pair arrives in a 4-slot ring of half tiles, loaded by the Q/dO producer
+    after each tile's Q/dO; slot 3 is the V tile's shared memory, free once V
+    is in TMEM.  K and V go
+    from their TMA
     tile into TMEM (the score MMAs' A operand) by the elementwise threads once
     KVFull completes; the MMA warp waits KVTmem before its first score."""
-    sim = _Sim(seed, slow_roles=slow_roles)
+    sim = _Sim(seed, slow_tma, slow_roles)
     for n, c in (("KVFull", 1), ("KVTmem", 2), ("DQFull", 1), ("DQEmpty", 4), ("Final", 1)):
         sim.bar(n, c)
     for i in range(2):
         for n, c in (("QFull", 1), ("QEmpty", 1), ("SFull", 1), ("PFull", 1), ("DSEmpty", 4), ("TileFull", 1),
                      ("TileEmpty", 2)):
             sim.bar(f"{n}{i}", c)
-    for i in range(3):
+    for i in range(4):
         sim.bar(f"PairFull{i}")
         sim.bar(f"PairEmpty{i}")
     stored, drained, lse_reads, pair_reads, staged = set(), {}, {}, set(), set()
@@ -292,15 +295,22 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None, slow_roles
             sim.asyncs.append((landq, f"QFull{s}"))
             if pair:
                 for h in range(2):
-                    n = 2 * t + h
-                    if n >= 3:
-                        yield _wait(plant, f"PairEmpty{n % 3}", n // 3 - 1)
+                    yield from load_pair(2 * t + h)
 
-                    def landp(n=n):
-                        if n >= 3 and (n - 3) not in pair_reads:
-                            raise ProtocolBug(f"pair slot {n % 3} reloaded before half {n - 3} read it")
-                        sim.mem[f"pair{n % 3}"] = n
-                    sim.asyncs.append((landp, f"PairFull{n % 3}"))
+    def load_pair(n):
+        slot = n % 4
+        if n >= 4:
+            yield _wait(plant, f"PairEmpty{slot}", n // 4 - 1)
+        if n == 3:   # slot 3 is V's shared tile: free once V is in TMEM
+            yield _wait(plant, "KVTmem", 0)
+
+        def landp(n=n, slot=slot):
+            if n >= 4 and (n - 4) not in pair_reads:
+                raise ProtocolBug(f"pair slot {slot} reloaded before half {n - 4} read it")
+            if slot == 3 and sim.mem.get("KVT1") != "kv":
+                raise ProtocolBug("pair slot 3 overwrites V before it was copied into TMEM")
+            sim.mem[f"pair{slot}"] = n
+        sim.asyncs.append((landp, f"PairFull{slot}"))
 
     def mma():
         yield ("wait", "KVFull", 0)
@@ -392,14 +402,14 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None, slow_roles
                 yield _wait(plant, f"DSEmpty{t & 1}", (t >> 1) - 1)
             n = 2 * t + h
             if pair:
-                yield _wait(plant, f"PairFull{n % 3}", n // 3)
+                yield _wait(plant, f"PairFull{n % 4}", n // 4)
 
             def ew(t=t, h=h, n=n):
                 sim.expect(f"lse{t & 1}", t)
                 lse_reads.setdefault(t, set()).add(h)
                 sim.expect(f"S{h}", ("S", t))
                 if pair:
-                    sim.expect(f"pair{n % 3}", n)
+                    sim.expect(f"pair{n % 4}", n)
                     pair_reads.add(n)
                 old = sim.mem.get(f"ds{t & 1}{h}")
                 if old is not None and (old != ("stg", t - 2) or (t - 2) not in staged):
@@ -409,7 +419,7 @@ def backward(T: int, pair: bool, seed: int, plant: str | None = None, slow_roles
             yield ("do", ew)
             yield ("arrive", f"TileEmpty{t & 1}")
             if pair:
-                yield ("arrive", f"PairEmpty{n % 3}")
+                yield ("arrive", f"PairEmpty{n % 4}")
             yield ("arrive", f"PFull{h}")
 
     def dq_warp(w):

@@ -18,10 +18,11 @@ def test_forward_protocol(pair):
 
 
 @pytest.mark.parametrize("pair", [False, True])
-def test_backward_protocol(pair):
+@pytest.mark.parametrize("slow_tma", [False, True])
+def test_backward_protocol(pair, slow_tma):
     for tiles in range(1, 7):
         for seed in range(40):
-            kp.backward(tiles, pair, seed)
+            kp.backward(tiles, pair, seed, slow_tma=slow_tma)
 
 
 def _caught(fn, plant, **kw):
@@ -39,12 +40,27 @@ def test_forward_planted_mistake_is_caught(plant):
     assert _caught(kp.forward, plant, n_kt=5, pair=True)
 
 
-@pytest.mark.parametrize("plant", ["QEmpty0", "DSEmpty0", "DQEmpty", "PairEmpty0", "bulk_wait_read0", "TileEmpty0",
-                                   "SFull1", "PFull1", "QFull1", "DQFull", "TileFull0", "PairFull1", "KVTmem"])
+@pytest.mark.parametrize("plant", ["QEmpty0", "DSEmpty0", "DQEmpty", "bulk_wait_read0", "TileEmpty0",
+                                   "SFull1", "PFull1", "QFull1", "DQFull", "TileFull0", "PairFull1", "KVTmem",
+                                   "PairFull3"])
 def test_backward_planted_mistake_is_caught(plant):
-    assert (_caught(kp.backward, plant, T=5, pair=True)
-            or _caught(kp.backward, plant, T=5, pair=True, slow_roles=("provider",))
-            or _caught(kp.backward, plant, T=5, pair=True, slow_roles=("dq0", "dq1", "dq2", "dq3")))
+    kw = dict(T=5, pair=True)
+    assert (_caught(kp.backward, plant, **kw)
+            or _caught(kp.backward, plant, slow_roles=("provider",), **kw)
+            or _caught(kp.backward, plant, slow_roles=("dq0", "dq1", "dq2", "dq3"), **kw)
+            or _caught(kp.backward, plant, slow_tma=True, **kw)
+            or _caught(kp.backward, plant, slow_roles=("ew0", "ew1"), **kw))
+
+
+@pytest.mark.parametrize("plant", ["PairEmpty0", "PairEmpty3"])
+def test_backward_pair_empty_is_implied(plant):
+    """With the pair halves of tile t issued by the Q/dO producer after its
+    QEmpty(t-2) wait, the products of tile t-2 -- and so the elementwise reads
+    of pair halves 2t-4 and 2t-3, the previous contents of the two slots --
+    are already done: the PairEmpty waits never wait (the model finds no
+    hazard without them).  The kernel keeps them as a guard."""
+    for kw in (dict(), dict(slow_tma=True), dict(slow_roles=("ew0", "ew1"))):
+        assert not _caught(kp.backward, plant, T=5, pair=True, **kw)
 
 
 def test_backward_per_half_store_wait_is_implied():
