@@ -20,9 +20,11 @@
 // dq_acc[t] += scale·dQ_t: the dQ warps stage the fp32 rows in the tile's
 // consumed dS buffer (128-byte swizzle) and add them with TMA reduce-adds.
 //   dpair[j, i] = dSᵀ (the reference's dpair = dS/scale with its dS ∘ scale),
-//                 written per head as key-major dS tiles, see pair_tiles.cu:
-//                 the MMA warp stores each finished dS half from shared memory
-//                 with one TMA store (the buffer's layout is the tile's box).
+//                 written per head as key-major dS tiles, see pair_tiles.cu
+//                 (through the per-head entry points: straight into the
+//                 caller's [B·H][KL][QL] dpair): the MMA warp stores each
+//                 finished dS half from shared memory with one TMA store (the
+//                 buffer's layout is the tile's box).
 // The pair bias is read in the elementwise step from the key-major per-head
 // copy pair_tiles() writes: each half tile [128 keys][64 queries] is one TMA
 // box (128-byte swizzle), so a thread reads its key's 16 queries as two
