@@ -419,7 +419,7 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     } else {
         // ------------------------------------------------------ dQ reductions
         // warp wi: E columns 32wi..32wi+31 of dQᵀ (TMEM lanes); thread = one E
-        // column, 64 query values.  Two rounds of one [32 queries][32 E] fp32
+        // column, 64 query values.  Two passes of one [32 queries][32 E] fp32
         // box per warp (128-byte swizzle) staged in the step's consumed dS
         // buffer, each added to dq_acc with one TMA reduce-add (rows past QL
         // are clipped by the tensor map).
@@ -440,7 +440,7 @@ fa_bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
             uint8_t* stg = smem + Lay::kDS + w * Lay::kDSBytes + wi * 4096;
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                if (r == 1 && lane == 0) bulk_wait_read<0>();   // round 0's box has been read
+                if (r == 1 && lane == 0) bulk_wait_read<0>();   // the first box has been read
                 __syncwarp();
 #pragma unroll
                 for (int qq = 0; qq < 32; ++qq)
